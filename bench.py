@@ -1,0 +1,344 @@
+"""Decode benchmark: Llama-2-7B-shaped int8 model, batch 1, on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one decode token (the hot path: TransformerEngine::forward_single_token
+of the reference) at batch 1.  Workload: random-init int8 weights (seed 0)
+generated on the device, a 512-token random prompt processed first (untimed),
+then W warm-up and K timed greedy decode steps with an fp16 KV cache.  The
+7.4 GB of weights read per step are 59x the 126 MB L2, so no flush is needed.
+
+value   tokens/s of all ranks (each rank decodes its own sequence; one JSON line
+        from rank 0), device-timed with CUDA events on the engine's stream,
+        max over ranks.
+e2e     the same metric through the reference-facing API with host buffers:
+        bt_engine_forward_token with the token id copied host->device and the
+        32000 fp32 logits copied device->host every step.
+roofline  algorithmic HBM bytes per step (weights + norms + embedding row + KV
+        read/write) / step time, against the measured copy bandwidth; plus the
+        dominant kernel (gate/up GEMV) timed per launch with events.
+cpu_baseline  the reference's own CPU engine (oracle/_ref/libbtref.so; falls
+        back to the C restatement) timed for a few 7B decode tokens on rank 0.
+
+--impl reference times the reference CPU implementation of the same step
+(rank 0 only) and prints the same JSON line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tokens/s and % HBM roofline at 1/2/4/8 B200 (7B int8, batch 1)"
+PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_HBM = 6650.0
+
+
+def hbm_peak():
+    try:
+        with open(PEAKS_FILE) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.out = os.path.join("/tmp", f"bt_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.f = open(self.out, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.out) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = max(mx, float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        os.unlink(self.out)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ---------------------------------------------------------------- CPU reference
+
+def cpu_reference_tokens_per_s(n_tokens: int, warmup: int, budget_s: float, log=print):
+    """Time the reference CPU engine on the 7B-shaped model (seed 0)."""
+    from oracle import oracle as O
+    from blocktensor_b200 import synthetic
+    shape = synthetic.SHAPES["llama2-7b"]
+    max_seq = warmup + n_tokens + 2
+    ocfg = O.make_config(*shape, max_seq)
+    t0 = time.time()
+    m = O.Model(ocfg, seed=0)
+    log(f"[cpu] 7B weights generated on the host in {time.time() - t0:.1f} s")
+    kind = "reference" if O.ref_available() else "port"
+    if kind == "reference":
+        eng = O.RefEngine(O.RefLib(), m, kv_max_seq=max_seq)
+        step = lambda t, p: eng.forward(t, p)
+    else:
+        kv = O.KV(ocfg, max_seq)
+        step = lambda t, p: O.forward_token(m, kv, t, p, nthreads=1)
+    prompt = synthetic.tokens(0, 1, shape[0])
+    tok, pos = int(prompt[0]), 0
+    for _ in range(warmup):
+        tok = int(np.argmax(step(tok, pos)))
+        pos += 1
+    done, t0 = 0, time.perf_counter()
+    while done < n_tokens:
+        tok = int(np.argmax(step(tok, pos)))
+        pos += 1
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return done / dt, kind, done, pos
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    n = max(1, min(args.steps, 3))
+    w = min(args.warmup, 1)
+    tps, kind, done, pos = cpu_reference_tokens_per_s(n, w, budget_s=90.0, log=lambda *a: print(*a, file=sys.stderr))
+    sample = (f"{done} decode tokens of the 7B-shaped int8 model after {w} warm-up token(s), context {pos - done + 1}-{pos} "
+              f"(attention is <1% of the CPU step at contexts below 1k)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": done, "warmup": w, "ms_per_step": 1000.0 / tps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "llama2-7b-shaped int8 decode, batch 1 (reference CPU backend)",
+                   "vocab": 32000, "dim": 4096, "hidden": 11008, "layers": 32, "heads": 32, "head_dim": 128},
+        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": 1, "kind": kind, "sample": sample},
+        "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- CUDA arm
+
+def run_ours(args):
+    import torch
+    import blocktensor_b200 as bt
+    from blocktensor_b200 import synthetic
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        pg = dist
+
+    def log(*a):
+        if rank == 0:
+            print(*a, file=sys.stderr, flush=True)
+
+    shape = args.model
+    prompt_len, W, K = args.prompt, args.warmup, args.steps
+    max_seq = prompt_len + W + K + args.e2e_steps + args.profile_steps + 2
+    cfg = synthetic.config(shape, max_seq)
+    t0 = time.time()
+    eng = bt.TransformerEngine(cfg, device=local, rope_theta=synthetic.ROPE_THETA[shape])
+    eng.generate(seed=0, sigma=0.02)
+    kv = bt.KVCache(eng, max_seq, bt.BT_KV_FP16)
+    log(f"[ours] {shape}: weights generated on device in {time.time() - t0:.1f} s")
+    prompt = synthetic.tokens(rank, prompt_len, cfg.vocab_size)
+    t0 = time.time()
+    eng.begin(kv, prompt)
+    eng.steps(kv, prompt_len)          # prompt, one position per step (untimed)
+    eng.steps(kv, W)                   # warm-up decode steps
+    torch.cuda.synchronize()
+    log(f"[ours] prompt {prompt_len} + warm-up {W} steps in {time.time() - t0:.1f} s")
+
+    stream = torch.cuda.ExternalStream(eng.stream_handle, device=torch.device("cuda", local))
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    pos0 = prompt_len + W
+    clocks = ClockSampler(local)
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    launches0 = bt.launch_count()
+    clocks.start()
+    ev0.record(stream)
+    eng.steps(kv, K, stream=eng.stream_handle)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if pg:
+        pg.barrier()
+    launches = bt.launch_count() - launches0
+    ms = ev0.elapsed_time(ev1)
+    if pg:
+        t = torch.tensor([ms], device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / K
+    value = world * K / (ms / 1000.0)
+
+    # algorithmic bytes per step, averaged over the timed contexts
+    kvb = 2
+    bytes_avg = sum(synthetic.step_bytes(cfg, pos0 + i + 1, kvb) for i in range(K)) / K
+    peak, peak_kind = hbm_peak()
+    achieved = bytes_avg / (ms_step / 1000.0) / 1e9
+
+    # end to end through the reference-facing call with host buffers
+    E = args.e2e_steps
+    logits = torch.empty(cfg.vocab_size, dtype=torch.float32).pin_memory()
+    tok_state = kv.state()[1]
+    pos = pos0 + K
+    import ctypes
+    am = ctypes.c_uint32()
+    lib = bt.load()
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    t0 = time.perf_counter()
+    tok = tok_state
+    for i in range(E):
+        bt.native.check(lib.bt_engine_forward_token(eng.handle, kv.handle, tok, pos + i,
+                                                    logits.data_ptr(), ctypes.byref(am)))
+        tok = am.value
+    e2e_s = time.perf_counter() - t0
+    if pg:
+        t = torch.tensor([e2e_s], device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = world * E / e2e_s
+
+    # dominant kernel per launch (eager, events around every launch)
+    prof = eng.profile(kv, args.profile_steps)
+    L, D, F = cfg.num_layers, cfg.dim, cfg.hidden_dim
+    gu_ms = prof["gateup"] / (args.profile_steps * L)
+    gu_bytes = 2 * F * D * (1 + 4 / 32) + 4 * D * 2
+    step_prof_ms = sum(prof.values()) / args.profile_steps
+    kernels = {k: round(v / args.profile_steps * 1000.0, 1) for k, v in prof.items()}  # us per step
+
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", "decode_step_traffic.json")
+    if os.path.exists(tfile):
+        try:
+            traffic = json.load(open(tfile)).get(shape)
+        except Exception:
+            traffic = None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            tps, kind, done, p = cpu_reference_tokens_per_s(2, 1, budget_s=45.0, log=log)
+            cpu = {"value": tps, "unit": "tokens/s", "cores": 1, "kind": kind,
+                   "sample": f"{done} decode tokens of the same 7B-shaped model on one host thread "
+                             f"(the reference engine is single-threaded), context {p - done + 1}-{p}"}
+        except Exception as ex:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": "tokens/s", "cores": 1, "kind": "reference",
+                   "sample": f"unavailable: {type(ex).__name__}: {ex}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"{shape}-shaped int8 decode, batch 1 per GPU", "model": shape,
+                       "global_batch": world, "seq_len": prompt_len, "prompt": prompt_len, "decode_steps": K,
+                       "kv_cache": "fp16", "activations": "fp32", "weights": "int8 Q8_0 (fp32 scale per 32)",
+                       "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (7.4 GB of weights per step)"},
+            "roofline": {"kernel": "decode_step", "bound": "hbm", "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
+                         "bytes_per_step": bytes_avg, "traffic": traffic,
+                         "dominant_kernel": {"name": "gateup (RMSNorm + [Wg;Wu] int8 GEMV + SwiGLU)",
+                                             "us_per_launch": gu_ms * 1000.0,
+                                             "achieved": gu_bytes / (gu_ms / 1000.0) / 1e9,
+                                             "frac": gu_bytes / (gu_ms / 1000.0) / 1e9 / peak,
+                                             "bytes_per_launch": gu_bytes},
+                         "eager_us_per_step_by_kernel": kernels, "eager_ms_per_step": step_prof_ms},
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 32,
+                    "d2h_bytes_per_step": cfg.vocab_size * 4 + 32,
+                    "api": "bt_engine_forward_token(host token, host logits)"},
+            "gpu_launches": launches,
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    kv.close()
+    eng.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", default="llama2-7b")
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--e2e-steps", type=int, default=64)
+    ap.add_argument("--profile-steps", type=int, default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

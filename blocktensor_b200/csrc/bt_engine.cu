@@ -1,0 +1,918 @@
+// bt_engine.cu -- the device-resident single-token decode engine.
+//
+// Replaces TransformerEngine::forward_single_token
+// (runtime/src/transformer_engine.cpp:228-251) for the CUDA backend.  One
+// token is 5 launches per layer plus one for the head, captured once in a
+// CUDA graph and replayed with the position and token in device memory:
+//
+//   qkv   : RMSNorm(x) -> [Wq;Wk;Wv] GEMV -> RoPE -> q, K/V cache append   (:117-146)
+//   attn  : split-K flash-decode over the cache, last CTA per KV head combines (:148-184)
+//   oproj : Wo GEMV -> x += o                                             (:186-195)
+//   gateup: RMSNorm(x) -> [Wg;Wu] GEMV -> silu(g)*u                       (:197-215)
+//   down  : Wd GEMV -> x += d                                             (:217-225)
+//   head  : RMSNorm(x) -> Whead GEMV -> logits, greedy argmax, next token (:244-250)
+//
+// Layer 0's qkv reads the embedding row of the current token directly
+// (:233-238) instead of copying the whole table to the host.
+#include "bt_common.cuh"
+#include "bt_gemv.cuh"
+#include "bt_internal.h"
+
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+namespace bt {
+
+// ---------------------------------------------------------------- attention
+
+struct AttnArgs {
+    const float* q;       // [H][hd] (after RoPE)
+    const void* k;        // layer base [KVH][max_seq][hd]
+    const void* v;
+    float* out;           // [H][hd]
+    float* part;          // [H][S][hd + 2]: m, l, o[hd]
+    uint32_t* ticket;     // [KVH]
+    const DevState* st;
+    uint32_t hd, G, max_seq, lmax;
+    float scale;          // 1/sqrt(hd) (transformer_engine.cpp:158)
+};
+
+// Grid (KVH, S): CTA (kvh, s) handles the G query heads of kv head kvh
+// (GQA map h / (H/KVH), transformer_engine.cpp:161) over keys
+// [s*L, min(c, (s+1)*L)), L = ceil(c/S), c = pos + 1.  It writes an
+// unnormalised partial (max m, sum l, o = sum e^(s-m) v); the last CTA of a
+// KV head (atomic ticket) merges the S partials.
+template <int NV, int GT, typename KVT>
+__global__ void __launch_bounds__(128) attn_decode_kernel(AttnArgs a) {
+    extern __shared__ float sm[];
+    __shared__ float s_m[16], s_l[16];
+    __shared__ bool s_last;
+    pdl_trigger();
+    pdl_wait();
+    const uint32_t kvh = blockIdx.x, sidx = blockIdx.y, S = gridDim.y;
+    const uint32_t HD = a.hd, G = a.G;
+    const uint32_t c = min(a.st->pos + 1, a.max_seq);
+    const uint32_t L = (c + S - 1) / S;
+    const uint32_t t0 = sidx * L;
+    const uint32_t t1 = min(c, t0 + L);
+    const uint32_t nk = t1 > t0 ? t1 - t0 : 0;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+
+    float* qs = sm;                 // [G][HD]
+    float* sc = sm + G * HD;        // [G][lmax]
+    for (uint32_t i = threadIdx.x; i < G * HD; i += blockDim.x) qs[i] = a.q[(size_t)kvh * G * HD + i];
+    __syncthreads();
+
+    const KVT* kb = reinterpret_cast<const KVT*>(a.k) + (size_t)kvh * a.max_seq * HD;
+    const KVT* vb = reinterpret_cast<const KVT*>(a.v) + (size_t)kvh * a.max_seq * HD;
+
+    // scores: one warp per key, lanes over head dims
+    for (uint32_t t = warp; t < nk; t += nw) {
+        const KVT* kr = kb + (size_t)(t0 + t) * HD;
+        float kv[NV];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const uint32_t d = lane + 32 * i;
+            kv[i] = d < HD ? KVConv<KVT>::to_f(kr[d]) : 0.0f;
+        }
+#pragma unroll
+        for (uint32_t g = 0; g < GT; ++g) {
+            if (g >= G) break;
+            float p = 0.0f;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const uint32_t d = lane + 32 * i;
+                if (d < HD) p = fmaf(qs[g * HD + d], kv[i], p);
+            }
+            p = warp_sum(p);
+            if (lane == 0) sc[g * a.lmax + t] = __fmul_rn(p, a.scale);
+        }
+    }
+    __syncthreads();
+    // per query head: running max and sum of exponentials (cpu_ref.hpp:55-72)
+    for (uint32_t g = warp; g < G; g += nw) {
+        float m = -INFINITY;
+        for (uint32_t t = lane; t < nk; t += 32) m = fmaxf(m, sc[g * a.lmax + t]);
+        m = warp_max(m);
+        float l = 0.0f;
+        for (uint32_t t = lane; t < nk; t += 32) {
+            const float e = expf(sc[g * a.lmax + t] - m);
+            sc[g * a.lmax + t] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        if (lane == 0) { s_m[g] = m; s_l[g] = l; }
+    }
+    __syncthreads();
+    // o = sum_t p_t v_t, threads over head dims
+    const size_t pstride = HD + 2;
+    for (uint32_t d = threadIdx.x; d < HD; d += blockDim.x) {
+        float acc[GT];
+#pragma unroll
+        for (int g = 0; g < GT; ++g) acc[g] = 0.0f;
+        for (uint32_t t = 0; t < nk; ++t) {
+            const float vv = KVConv<KVT>::to_f(vb[(size_t)(t0 + t) * HD + d]);
+#pragma unroll
+            for (int g = 0; g < GT; ++g)
+                if ((uint32_t)g < G) acc[g] = fmaf(sc[g * a.lmax + t], vv, acc[g]);
+        }
+#pragma unroll
+        for (int g = 0; g < GT; ++g)
+            if ((uint32_t)g < G) a.part[((size_t)(kvh * G + g) * S + sidx) * pstride + 2 + d] = acc[g];
+    }
+    if (threadIdx.x < G) {
+        float* p = a.part + ((size_t)(kvh * G + threadIdx.x) * S + sidx) * pstride;
+        p[0] = s_m[threadIdx.x];
+        p[1] = s_l[threadIdx.x];
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = (atomicAdd(a.ticket + kvh, 1u) == S - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (uint32_t i = threadIdx.x; i < G * HD; i += blockDim.x) {
+        const uint32_t g = i / HD, d = i % HD;
+        const float* pb = a.part + (size_t)(kvh * G + g) * S * pstride;
+        float M = -INFINITY;
+        for (uint32_t s = 0; s < S; ++s)
+            if (__ldcg(pb + s * pstride + 1) > 0.0f) M = fmaxf(M, __ldcg(pb + s * pstride));
+        float l = 0.0f, o = 0.0f;
+        for (uint32_t s = 0; s < S; ++s) {
+            const float ls = __ldcg(pb + s * pstride + 1);
+            if (ls > 0.0f) {
+                const float f = expf(__ldcg(pb + s * pstride) - M);
+                l = fmaf(ls, f, l);
+                o = fmaf(__ldcg(pb + s * pstride + 2 + d), f, o);
+            }
+        }
+        a.out[(size_t)(kvh * G + g) * HD + d] = __fdiv_rn(o, l);
+    }
+    if (threadIdx.x == 0) a.ticket[kvh] = 0;
+}
+
+template <int NV, int GT, typename KVT>
+static cudaError_t launch_attn_g(const AttnArgs& a, uint32_t KVH, uint32_t S, cudaStream_t s, bool pdl) {
+    auto kern = attn_decode_kernel<NV, GT, KVT>;
+    const size_t smem = (size_t)(a.G * a.hd + a.G * a.lmax) * sizeof(float);
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    return launch_pdl(kern, dim3(KVH, S), dim3(128), smem, s, pdl, a);
+}
+
+template <int NV, typename KVT>
+static cudaError_t launch_attn_t(const AttnArgs& a, uint32_t KVH, uint32_t S, cudaStream_t s, bool pdl) {
+    if (a.G <= 1) return launch_attn_g<NV, 1, KVT>(a, KVH, S, s, pdl);
+    if (a.G <= 2) return launch_attn_g<NV, 2, KVT>(a, KVH, S, s, pdl);
+    if (a.G <= 4) return launch_attn_g<NV, 4, KVT>(a, KVH, S, s, pdl);
+    if (a.G <= 8) return launch_attn_g<NV, 8, KVT>(a, KVH, S, s, pdl);
+    return launch_attn_g<NV, 16, KVT>(a, KVH, S, s, pdl);
+}
+
+template <typename KVT>
+static cudaError_t launch_attn(const AttnArgs& a, uint32_t KVH, uint32_t S, cudaStream_t s, bool pdl) {
+    const uint32_t nv = (a.hd + 31) / 32;
+    if (nv <= 1) return launch_attn_t<1, KVT>(a, KVH, S, s, pdl);
+    if (nv <= 2) return launch_attn_t<2, KVT>(a, KVH, S, s, pdl);
+    if (nv <= 4) return launch_attn_t<4, KVT>(a, KVH, S, s, pdl);
+    return launch_attn_t<8, KVT>(a, KVH, S, s, pdl);
+}
+
+}  // namespace bt
+
+using namespace bt;
+
+// ---------------------------------------------------------------- engine objects
+
+struct LayerDev {
+    int8_t* qkv_q; float* qkv_s;   // [D + 2 KVD][D]   q,k rows RoPE-pair interleaved
+    int8_t* o_q;   float* o_s;     // [D][D]
+    int8_t* gu_q;  float* gu_s;    // [2F][D]          (gate, up) rows interleaved
+    int8_t* d_q;   float* d_s;     // [D][F]
+    float* attn_norm;
+    float* ffn_norm;
+};
+
+struct bt_engine {
+    int device = 0;
+    bt_model_config cfg{};
+    float theta = 10000.0f;
+    cudaStream_t stream = nullptr;
+    bool pdl = true;
+    bool use_graph = true;
+    bool taps_on = false;
+    std::vector<void*> allocs;
+    std::vector<LayerDev> layers;
+    float* embed = nullptr;
+    float* out_norm = nullptr;
+    int8_t* head_q = nullptr;
+    float* head_s = nullptr;
+    // activations
+    float* x = nullptr;
+    float* q = nullptr;
+    float* attn = nullptr;
+    float* act = nullptr;
+    float* logits = nullptr;
+    float* taps = nullptr;
+    // argmax scratch
+    float* am_val = nullptr;
+    uint32_t* am_idx = nullptr;
+    uint32_t* am_ticket = nullptr;
+    bool loaded = false;
+};
+
+struct bt_kv {
+    bt_engine* e = nullptr;
+    uint32_t max_seq = 0;
+    int dtype = BT_KV_FP32;
+    std::vector<void*> allocs;
+    void* k = nullptr;          // [L][KVH][max_seq][hd]
+    void* v = nullptr;
+    float2* rope = nullptr;     // [max_seq][hd/2]
+    DevState* st = nullptr;
+    uint32_t* tok_hist = nullptr;  // [max_seq + 1]
+    float* att_part = nullptr;
+    uint32_t* att_ticket = nullptr;
+    uint32_t splits = 1, lmax = 1;
+    DevState* h_st = nullptr;   // pinned staging
+    uint64_t host_pos = 0;      // position of the next step, mirrored on the host for bounds checks
+    cudaGraphExec_t graph = nullptr;
+    bool graph_taps = false;
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+template <typename T>
+int dev_alloc(std::vector<void*>& list, T** out, size_t count, const char* what) {
+    void* p = nullptr;
+    const size_t bytes = count * sizeof(T);
+    cudaError_t e = cudaMalloc(&p, bytes ? bytes : 16);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(e == cudaErrorMemoryAllocation ? BT_ERR_OUT_OF_MEMORY : BT_ERR_CUDA,
+                    std::string("cudaMalloc(") + what + ", " + std::to_string(bytes) + " B): " + cudaGetErrorString(e));
+    }
+    list.push_back(p);
+    *out = static_cast<T*>(p);
+    return BT_OK;
+}
+
+#define BT_TRY_ALLOC(list, ptr, count, what)                         \
+    do {                                                             \
+        int _rc = dev_alloc(list, ptr, count, what);                 \
+        if (_rc != BT_OK) return _rc;                                \
+    } while (0)
+
+uint32_t kvd(const bt_model_config& c) { return c.num_kv_heads * c.head_dim; }
+
+int validate_config(const bt_model_config& c) {
+    if (c.vocab_size == 0 || c.dim == 0 || c.hidden_dim == 0 || c.num_layers == 0 || c.num_heads == 0 ||
+        c.num_kv_heads == 0 || c.head_dim == 0)
+        return fail(BT_ERR_INVALID_ARGUMENT, "model config: zero-sized dimension");
+    if (c.dim % 32 || c.hidden_dim % 32)
+        return fail(BT_ERR_INVALID_ARGUMENT, "model config: dim and hidden_dim must be multiples of 32 (Q8_0 blocks)");
+    if (c.num_heads * c.head_dim != c.dim)
+        return fail(BT_ERR_INVALID_ARGUMENT, "model config: num_heads * head_dim must equal dim");
+    if (c.num_heads % c.num_kv_heads)
+        return fail(BT_ERR_INVALID_ARGUMENT, "model config: num_heads must be a multiple of num_kv_heads");
+    if (c.head_dim % 2 || c.head_dim > 256)
+        return fail(BT_ERR_INVALID_ARGUMENT, "model config: head_dim must be even and <= 256");
+    if (c.num_heads / c.num_kv_heads > 16)
+        return fail(BT_ERR_INVALID_ARGUMENT, "model config: at most 16 query heads per KV head");
+    if (c.dim > 48 * 1024 || c.hidden_dim > 48 * 1024)
+        return fail(BT_ERR_INVALID_ARGUMENT, "model config: dim/hidden_dim above 49152 not supported");
+    return BT_OK;
+}
+
+// Destination of each of the 9 per-layer tensors inside the fused device layout.
+struct Slot {
+    int8_t* q;
+    float* s;
+    uint32_t rows, cols;
+    RowMap map;
+};
+
+Slot layer_slot(bt_engine* e, uint32_t l, int j) {
+    const auto& c = e->cfg;
+    LayerDev& L = e->layers[l];
+    const uint32_t D = c.dim, F = c.hidden_dim, KV = kvd(c), hd = c.head_dim;
+    switch (j) {
+        case 2: return {L.qkv_q, L.qkv_s, D, D, RowMap{1, hd, 0, 0, 0}};
+        case 3: return {L.qkv_q, L.qkv_s, KV, D, RowMap{1, hd, 0, 0, D}};
+        case 4: return {L.qkv_q, L.qkv_s, KV, D, RowMap{0, 0, 0, 0, D + KV}};
+        case 5: return {L.o_q, L.o_s, D, D, RowMap{0, 0, 0, 0, 0}};
+        case 6: return {L.gu_q, L.gu_s, F, D, RowMap{2, 0, 0, 0, 0}};
+        case 7: return {L.gu_q, L.gu_s, F, D, RowMap{2, 0, 1, 0, 0}};
+        default: return {L.d_q, L.d_s, D, F, RowMap{0, 0, 0, 0, 0}};
+    }
+}
+
+int alloc_weights(bt_engine* e) {
+    const auto& c = e->cfg;
+    const size_t D = c.dim, F = c.hidden_dim, KV = kvd(c), V = c.vocab_size;
+    auto& A = e->allocs;
+    BT_TRY_ALLOC(A, &e->embed, V * D, "embed");
+    BT_TRY_ALLOC(A, &e->out_norm, D, "out_norm");
+    BT_TRY_ALLOC(A, &e->head_q, V * D, "head qs");
+    BT_TRY_ALLOC(A, &e->head_s, V * D / 32, "head scales");
+    e->layers.resize(c.num_layers);
+    for (uint32_t l = 0; l < c.num_layers; ++l) {
+        LayerDev& L = e->layers[l];
+        const size_t Mqkv = D + 2 * KV;
+        BT_TRY_ALLOC(A, &L.qkv_q, Mqkv * D, "wqkv");
+        BT_TRY_ALLOC(A, &L.qkv_s, Mqkv * D / 32, "wqkv scales");
+        BT_TRY_ALLOC(A, &L.o_q, D * D, "wo");
+        BT_TRY_ALLOC(A, &L.o_s, D * D / 32, "wo scales");
+        BT_TRY_ALLOC(A, &L.gu_q, 2 * F * D, "wgu");
+        BT_TRY_ALLOC(A, &L.gu_s, 2 * F * D / 32, "wgu scales");
+        BT_TRY_ALLOC(A, &L.d_q, D * F, "wd");
+        BT_TRY_ALLOC(A, &L.d_s, D * F / 32, "wd scales");
+        BT_TRY_ALLOC(A, &L.attn_norm, D, "attn_norm");
+        BT_TRY_ALLOC(A, &L.ffn_norm, D, "ffn_norm");
+    }
+    BT_TRY_ALLOC(A, &e->x, D, "x");
+    BT_TRY_ALLOC(A, &e->q, D, "q");
+    BT_TRY_ALLOC(A, &e->attn, D, "attn");
+    BT_TRY_ALLOC(A, &e->act, F, "act");
+    BT_TRY_ALLOC(A, &e->logits, V, "logits");
+    BT_TRY_ALLOC(A, &e->taps, (size_t)c.num_layers * D, "taps");
+    const size_t nblk = V + 1;  // one partial per CTA, at least one row per CTA
+    BT_TRY_ALLOC(A, &e->am_val, nblk, "argmax val");
+    BT_TRY_ALLOC(A, &e->am_idx, nblk, "argmax idx");
+    BT_TRY_ALLOC(A, &e->am_ticket, 4, "argmax ticket");
+    BT_CUDA_CHECK(cudaMemsetAsync(e->am_ticket, 0, 16, e->stream));
+    return BT_OK;
+}
+
+void drop_graphs_of(bt_kv* kv) {
+    if (kv->graph) {
+        cudaGraphExecDestroy(kv->graph);
+        kv->graph = nullptr;
+    }
+}
+
+// Events recorded after every launch of a step (per-kernel profiling; no PDL).
+struct Marks {
+    cudaEvent_t* ev;
+    int n;
+};
+
+#define BT_MARK()                                                   \
+    do {                                                            \
+        if (marks) BT_CUDA_CHECK(cudaEventRecord(marks->ev[marks->n++], s)); \
+    } while (0)
+
+// Enqueue one decode step (all launches) on stream s.
+int enqueue_step(bt_engine* e, bt_kv* kv, cudaStream_t s, Marks* marks = nullptr) {
+    const auto& c = e->cfg;
+    const uint32_t D = c.dim, F = c.hidden_dim, KV = kvd(c), hd = c.head_dim;
+    const uint32_t G = c.num_heads / c.num_kv_heads;
+    const bool pdl = e->pdl && !marks;
+    const size_t kv_layer = (size_t)c.num_kv_heads * kv->max_seq * hd;
+    const size_t esz = kv->dtype == BT_KV_FP16 ? 2 : 4;
+    const float scale = 1.0f / std::sqrt((float)hd);
+    for (uint32_t l = 0; l < c.num_layers; ++l) {
+        const LayerDev& L = e->layers[l];
+        char* kl = static_cast<char*>(kv->k) + l * kv_layer * esz;
+        char* vl = static_cast<char*>(kv->v) + l * kv_layer * esz;
+        // qkv
+        {
+            GemvW g{L.qkv_q, L.qkv_s, D + 2 * KV, D};
+            ProNorm pro{e->x, L.attn_norm, c.rms_norm_eps, l == 0 ? e->embed : nullptr, kv->st, e->x};
+            cudaError_t err;
+            if (kv->dtype == BT_KV_FP16) {
+                EpiQKV<__half> epi{e->q, reinterpret_cast<__half*>(kl), reinterpret_cast<__half*>(vl), kv->rope, kv->st,
+                                   D, KV, hd, kv->max_seq};
+                err = launch_gemv(g, pro, epi, s, pdl, 4);
+            } else {
+                EpiQKV<float> epi{e->q, reinterpret_cast<float*>(kl), reinterpret_cast<float*>(vl), kv->rope, kv->st,
+                                  D, KV, hd, kv->max_seq};
+                err = launch_gemv(g, pro, epi, s, pdl, 4);
+            }
+            BT_CUDA_CHECK(err);
+            BT_MARK();
+        }
+        // attention
+        {
+            AttnArgs a{e->q, kl, vl, e->attn, kv->att_part, kv->att_ticket + l * c.num_kv_heads, kv->st,
+                       hd, G, kv->max_seq, kv->lmax, scale};
+            cudaError_t err = kv->dtype == BT_KV_FP16 ? launch_attn<__half>(a, c.num_kv_heads, kv->splits, s, pdl)
+                                                       : launch_attn<float>(a, c.num_kv_heads, kv->splits, s, pdl);
+            BT_CUDA_CHECK(err);
+            BT_MARK();
+        }
+        // o-proj + residual
+        BT_CUDA_CHECK(launch_gemv(GemvW{L.o_q, L.o_s, D, D}, ProCopy{e->attn}, EpiResidual{e->x, nullptr}, s, pdl));
+        BT_MARK();
+        // gate/up + SwiGLU
+        BT_CUDA_CHECK(launch_gemv(GemvW{L.gu_q, L.gu_s, 2 * F, D},
+                                  ProNorm{e->x, L.ffn_norm, c.rms_norm_eps, nullptr, nullptr, nullptr},
+                                  EpiSwiGLU{e->act}, s, pdl, 4));
+        BT_MARK();
+        // down + residual (+ tap)
+        BT_CUDA_CHECK(launch_gemv(GemvW{L.d_q, L.d_s, D, F}, ProCopy{e->act},
+                                  EpiResidual{e->x, e->taps_on ? e->taps + (size_t)l * D : nullptr}, s, pdl));
+        BT_MARK();
+    }
+    BT_CUDA_CHECK(launch_gemv(GemvW{e->head_q, e->head_s, c.vocab_size, D},
+                              ProNorm{e->x, e->out_norm, c.rms_norm_eps, nullptr, nullptr, nullptr},
+                              EpiLogits{e->logits, e->am_val, e->am_idx, e->am_ticket, kv->st, kv->tok_hist,
+                                        kv->max_seq},
+                              s, pdl));
+    BT_MARK();
+    return BT_OK;
+}
+
+int ensure_graph(bt_engine* e, bt_kv* kv) {
+    if (!e->use_graph) return BT_OK;
+    if (kv->graph && kv->graph_taps == e->taps_on) return BT_OK;
+    drop_graphs_of(kv);
+    // configure every kernel of the step (shared-memory attributes) outside capture
+    g_dry_run = true;
+    int drc = enqueue_step(e, kv, e->stream);
+    g_dry_run = false;
+    if (drc != BT_OK) return drc;
+    cudaGraph_t g = nullptr;
+    BT_CUDA_CHECK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(e, kv, e->stream);
+    cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+    if (rc != BT_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (ce != cudaSuccess) return fail(BT_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+    ce = cudaGraphInstantiate(&kv->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) {
+        kv->graph = nullptr;
+        return fail(BT_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ce));
+    }
+    kv->graph_taps = e->taps_on;
+    return BT_OK;
+}
+
+int run_steps(bt_engine* e, bt_kv* kv, uint32_t n, cudaStream_t s) {
+    if (kv->host_pos + n > kv->max_seq) return fail(BT_ERR_OUT_OF_RANGE, "KVCache pos out of bounds");
+    int rc = ensure_graph(e, kv);
+    if (rc != BT_OK) return rc;
+    for (uint32_t i = 0; i < n; ++i) {
+        if (e->use_graph) {
+            g_launches.fetch_add(5ull * e->cfg.num_layers + 1, std::memory_order_relaxed);
+            BT_CUDA_CHECK(cudaGraphLaunch(kv->graph, s));
+        } else {
+            rc = enqueue_step(e, kv, s);
+            if (rc != BT_OK) return rc;
+        }
+        kv->host_pos += 1;
+    }
+    return BT_OK;
+}
+
+int check_engine(bt_engine* e) {
+    if (!e) return fail(BT_ERR_INVALID_ARGUMENT, "null engine");
+    if (!e->loaded) return fail(BT_ERR_RUNTIME, "engine has no weights (call bt_engine_load or bt_engine_generate)");
+    return BT_OK;
+}
+
+int check_kv(bt_engine* e, bt_kv* kv) {
+    if (!kv) return fail(BT_ERR_INVALID_ARGUMENT, "null KV cache");
+    if (kv->e != e) return fail(BT_ERR_INVALID_ARGUMENT, "KV cache belongs to another engine");
+    return BT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bt_engine_create(int device, const bt_model_config* cfg, const bt_engine_options* opt, bt_engine** out) {
+    if (!cfg || !out) return fail(BT_ERR_INVALID_ARGUMENT, "bt_engine_create: null argument");
+    *out = nullptr;
+    int rc = validate_config(*cfg);
+    if (rc != BT_OK) return rc;
+    int ndev = 0;
+    BT_CUDA_CHECK(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return fail(BT_ERR_INVALID_ARGUMENT, "bt_engine_create: bad device index");
+    DeviceGuard guard(device);
+    auto e = std::make_unique<bt_engine>();
+    e->device = device;
+    e->cfg = *cfg;
+    if (opt && opt->rope_theta > 0.0f) e->theta = opt->rope_theta;
+    if (const char* v = std::getenv("BT_NO_PDL")) e->pdl = (v[0] == '0');
+    if (const char* v = std::getenv("BT_NO_GRAPH")) e->use_graph = (v[0] == '0');
+    BT_CUDA_CHECK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+    rc = alloc_weights(e.get());
+    if (rc != BT_OK) {
+        std::string msg = bt_cuda_last_error();
+        bt_engine_destroy(e.release());
+        set_error(msg);
+        return rc;
+    }
+    *out = e.release();
+    return BT_OK;
+}
+
+int bt_engine_destroy(bt_engine* e) {
+    if (!e) return BT_OK;
+    DeviceGuard guard(e->device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    for (void* p : e->allocs) cudaFree(p);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+    return BT_OK;
+}
+
+int bt_engine_load(bt_engine* e, const bt_tensor_view* t, uint32_t n, int on_device) {
+    if (!e || !t) return fail(BT_ERR_INVALID_ARGUMENT, "bt_engine_load: null argument");
+    const auto& c = e->cfg;
+    if (n != 3 + 9 * c.num_layers)
+        return fail(BT_ERR_INVALID_ARGUMENT, "bt_engine_load: expected 3 + 9*num_layers tensors");
+    DeviceGuard guard(e->device);
+    const size_t D = c.dim, F = c.hidden_dim, KV = kvd(c), V = c.vocab_size;
+    auto qbytes = [](size_t r, size_t k) { return r * k / 32 * 36; };
+    // size checks (the reference reads raw sizes; a mismatch is a corrupt model)
+    auto expect = [&](uint32_t i, size_t bytes, const char* what) -> int {
+        if (t[i].bytes != bytes || (!t[i].data && bytes))
+            return fail(BT_ERR_RUNTIME, std::string("bt_engine_load: tensor ") + std::to_string(i) + " (" + what +
+                                            ") has " + std::to_string(t[i].bytes) + " bytes, expected " +
+                                            std::to_string(bytes));
+        return BT_OK;
+    };
+    int rc;
+    if ((rc = expect(0, V * D * 4, "embed"))) return rc;
+    if ((rc = expect(1, D * 4, "out_norm"))) return rc;
+    if ((rc = expect(2, qbytes(V, D), "head"))) return rc;
+    for (uint32_t l = 0; l < c.num_layers; ++l) {
+        const size_t sizes[9] = {D * 4, D * 4, qbytes(D, D), qbytes(KV, D), qbytes(KV, D), qbytes(D, D),
+                                 qbytes(F, D), qbytes(F, D), qbytes(D, F)};
+        for (int j = 0; j < 9; ++j)
+            if ((rc = expect(3 + 9 * l + j, sizes[j], "layer tensor"))) return rc;
+    }
+    const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    cudaStream_t s = e->stream;
+    BT_CUDA_CHECK(cudaMemcpyAsync(e->embed, t[0].data, t[0].bytes, kind, s));
+    BT_CUDA_CHECK(cudaMemcpyAsync(e->out_norm, t[1].data, t[1].bytes, kind, s));
+    // staging buffer for 36-byte blocks (device copy when the source is on the host)
+    size_t max_q = qbytes(V, D);
+    for (size_t b : {qbytes(F, D), qbytes(D, F)}) max_q = b > max_q ? b : max_q;
+    void* stage = nullptr;
+    if (!on_device) BT_CUDA_CHECK(cudaMalloc(&stage, max_q));
+    auto load_q = [&](const bt_tensor_view& tv, int8_t* q, float* sc, uint32_t rows, uint32_t cols, RowMap m) -> int {
+        const void* src = tv.data;
+        if (!on_device) {
+            BT_CUDA_CHECK(cudaMemcpyAsync(stage, tv.data, tv.bytes, cudaMemcpyHostToDevice, s));
+            src = stage;
+        }
+        BT_CUDA_CHECK(launch_repack_q8_0(src, q, sc, rows, cols, m, s));
+        if (!on_device) BT_CUDA_CHECK(cudaStreamSynchronize(s));  // stage is reused
+        return BT_OK;
+    };
+    rc = load_q(t[2], e->head_q, e->head_s, c.vocab_size, c.dim, RowMap{0, 0, 0, 0, 0});
+    for (uint32_t l = 0; rc == BT_OK && l < c.num_layers; ++l) {
+        LayerDev& L = e->layers[l];
+        const bt_tensor_view* tl = t + 3 + 9 * l;
+        cudaError_t ce = cudaMemcpyAsync(L.attn_norm, tl[0].data, tl[0].bytes, kind, s);
+        if (ce == cudaSuccess) ce = cudaMemcpyAsync(L.ffn_norm, tl[1].data, tl[1].bytes, kind, s);
+        if (ce != cudaSuccess) { rc = fail(BT_ERR_CUDA, cudaGetErrorString(ce)); break; }
+        for (int j = 2; j < 9 && rc == BT_OK; ++j) {
+            Slot sl = layer_slot(e, l, j);
+            rc = load_q(tl[j], sl.q, sl.s, sl.rows, sl.cols, sl.map);
+        }
+    }
+    cudaError_t ce = cudaStreamSynchronize(s);
+    if (stage) cudaFree(stage);
+    if (rc != BT_OK) return rc;
+    if (ce != cudaSuccess) return fail(BT_ERR_CUDA, std::string("bt_engine_load: ") + cudaGetErrorString(ce));
+    e->loaded = true;
+    return BT_OK;
+}
+
+int bt_engine_generate(bt_engine* e, uint64_t seed, float sigma) {
+    if (!e) return fail(BT_ERR_INVALID_ARGUMENT, "bt_engine_generate: null engine");
+    DeviceGuard guard(e->device);
+    const auto& c = e->cfg;
+    const size_t D = c.dim, F = c.hidden_dim, KV = kvd(c), V = c.vocab_size;
+    const float k = normal_k(sigma);
+    cudaStream_t s = e->stream;
+    // slabs of at most 32M elements: fp32 values, then their 36-byte blocks
+    const size_t slab = 32u << 20;
+    float* tmp = nullptr;
+    void* blk = nullptr;
+    BT_CUDA_CHECK(cudaMalloc(&tmp, slab * sizeof(float)));
+    cudaError_t ce = cudaMalloc(&blk, slab / 32 * 36);
+    if (ce != cudaSuccess) {
+        cudaFree(tmp);
+        return fail(BT_ERR_OUT_OF_MEMORY, "bt_engine_generate: staging allocation failed");
+    }
+    int rc = BT_OK;
+    auto gen_q = [&](uint32_t stream_id, int8_t* q, float* sc, size_t rows, size_t cols, RowMap m) -> int {
+        const size_t rows_per = slab / cols;
+        for (size_t r0 = 0; r0 < rows; r0 += rows_per) {
+            const size_t nr = (rows - r0) < rows_per ? (rows - r0) : rows_per;
+            BT_CUDA_CHECK(launch_gen_normal(seed, stream_id, r0 * cols, nr * cols, k, tmp, s));
+            BT_CUDA_CHECK(launch_quantize_q8_0(tmp, blk, nr * cols / 32, s));
+            RowMap mm = m;
+            mm.src_off = (uint32_t)r0;
+            BT_CUDA_CHECK(launch_repack_q8_0(blk, q, sc, (uint32_t)nr, (uint32_t)cols, mm, s));
+        }
+        return BT_OK;
+    };
+    ce = launch_gen_normal(seed, 0, 0, V * D, k, e->embed, s);
+    if (ce == cudaSuccess) ce = launch_fill(e->out_norm, D, 1.0f, s);
+    if (ce != cudaSuccess) rc = fail(BT_ERR_CUDA, cudaGetErrorString(ce));
+    if (rc == BT_OK) rc = gen_q(2, e->head_q, e->head_s, V, D, RowMap{0, 0, 0, 0, 0});
+    for (uint32_t l = 0; rc == BT_OK && l < c.num_layers; ++l) {
+        LayerDev& L = e->layers[l];
+        ce = launch_fill(L.attn_norm, D, 1.0f, s);
+        if (ce == cudaSuccess) ce = launch_fill(L.ffn_norm, D, 1.0f, s);
+        if (ce != cudaSuccess) { rc = fail(BT_ERR_CUDA, cudaGetErrorString(ce)); break; }
+        for (int j = 2; j < 9 && rc == BT_OK; ++j) {
+            Slot sl = layer_slot(e, l, j);
+            rc = gen_q(16 + 16 * l + j, sl.q, sl.s, sl.rows, sl.cols, sl.map);
+        }
+    }
+    (void)KV; (void)F;
+    ce = cudaStreamSynchronize(s);
+    cudaFree(tmp);
+    cudaFree(blk);
+    if (rc != BT_OK) return rc;
+    if (ce != cudaSuccess) return fail(BT_ERR_CUDA, std::string("bt_engine_generate: ") + cudaGetErrorString(ce));
+    e->loaded = true;
+    return BT_OK;
+}
+
+int bt_kv_create(bt_engine* e, uint32_t max_seq, int dtype, bt_kv** out) {
+    if (!e || !out) return fail(BT_ERR_INVALID_ARGUMENT, "bt_kv_create: null argument");
+    if (max_seq == 0) return fail(BT_ERR_INVALID_ARGUMENT, "bt_kv_create: max_seq must be > 0");
+    if (dtype != BT_KV_FP32 && dtype != BT_KV_FP16) return fail(BT_ERR_INVALID_ARGUMENT, "bt_kv_create: bad kv dtype");
+    *out = nullptr;
+    DeviceGuard guard(e->device);
+    const auto& c = e->cfg;
+    auto kv = std::make_unique<bt_kv>();
+    kv->e = e;
+    kv->max_seq = max_seq;
+    kv->dtype = dtype;
+    const size_t esz = dtype == BT_KV_FP16 ? 2 : 4;
+    const size_t n = (size_t)c.num_layers * c.num_kv_heads * max_seq * c.head_dim;
+    auto cleanup = [&](int rc) {
+        std::string msg = bt_cuda_last_error();
+        bt_kv_destroy(kv.release());
+        set_error(msg);
+        return rc;
+    };
+    int rc;
+    uint8_t* kb = nullptr;
+    uint8_t* vb = nullptr;
+    if ((rc = dev_alloc(kv->allocs, &kb, n * esz, "K cache"))) return cleanup(rc);
+    if ((rc = dev_alloc(kv->allocs, &vb, n * esz, "V cache"))) return cleanup(rc);
+    kv->k = kb;
+    kv->v = vb;
+    const uint32_t half = c.head_dim / 2;
+    if ((rc = dev_alloc(kv->allocs, &kv->rope, (size_t)max_seq * half, "rope table"))) return cleanup(rc);
+    if ((rc = dev_alloc(kv->allocs, &kv->st, 1, "state"))) return cleanup(rc);
+    if ((rc = dev_alloc(kv->allocs, &kv->tok_hist, (size_t)max_seq + 1, "token history"))) return cleanup(rc);
+    // attention split count: >= 2 CTAs per SM over all KV heads, <= 256 keys per split
+    uint32_t S = (296 + c.num_kv_heads - 1) / c.num_kv_heads;
+    const uint32_t s2 = (max_seq + 255) / 256;
+    if (s2 > S) S = s2;
+    if (S > max_seq) S = max_seq;
+    if (S < 1) S = 1;
+    kv->splits = S;
+    kv->lmax = (max_seq + S - 1) / S;
+    if ((rc = dev_alloc(kv->allocs, &kv->att_part, (size_t)c.num_heads * S * (c.head_dim + 2), "attention partials")))
+        return cleanup(rc);
+    if ((rc = dev_alloc(kv->allocs, &kv->att_ticket, (size_t)c.num_layers * c.num_kv_heads, "attention tickets")))
+        return cleanup(rc);
+    cudaError_t ce = cudaMemsetAsync(kv->att_ticket, 0, sizeof(uint32_t) * c.num_layers * c.num_kv_heads, e->stream);
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(kb, 0, n * esz, e->stream);
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(vb, 0, n * esz, e->stream);
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(kv->st, 0, sizeof(DevState), e->stream);
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(kv->tok_hist, 0, sizeof(uint32_t) * (max_seq + 1), e->stream);
+    if (ce != cudaSuccess) return cleanup(fail(BT_ERR_CUDA, cudaGetErrorString(ce)));
+    // RoPE table with the reference formula (kernels/cpu_ref.hpp:40-43), host libm
+    std::vector<float2> tab((size_t)max_seq * half);
+    for (uint32_t i = 0; i < half; ++i) {
+        const float freq = 1.0f / std::pow(e->theta, (float)(2 * i) / (float)c.head_dim);
+        for (uint32_t p = 0; p < max_seq; ++p) {
+            const float val = (float)p * freq;
+            tab[(size_t)p * half + i] = make_float2(std::cos(val), std::sin(val));
+        }
+    }
+    ce = cudaMemcpyAsync(kv->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, e->stream);
+    if (ce == cudaSuccess) ce = cudaMallocHost(&kv->h_st, sizeof(DevState));
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->stream);
+    if (ce != cudaSuccess) return cleanup(fail(BT_ERR_CUDA, cudaGetErrorString(ce)));
+    *out = kv.release();
+    return BT_OK;
+}
+
+int bt_kv_destroy(bt_kv* kv) {
+    if (!kv) return BT_OK;
+    DeviceGuard guard(kv->e->device);
+    cudaStreamSynchronize(kv->e->stream);
+    drop_graphs_of(kv);
+    for (void* p : kv->allocs) cudaFree(p);
+    if (kv->h_st) cudaFreeHost(kv->h_st);
+    delete kv;
+    return BT_OK;
+}
+
+int bt_kv_read_layer(bt_kv* kv, uint32_t layer, float* k, float* v) {
+    if (!kv || !k || !v) return fail(BT_ERR_INVALID_ARGUMENT, "bt_kv_read_layer: null argument");
+    bt_engine* e = kv->e;
+    const auto& c = e->cfg;
+    if (layer >= c.num_layers) return fail(BT_ERR_OUT_OF_RANGE, "KVCache layer out of bounds");
+    DeviceGuard guard(e->device);
+    const size_t per = (size_t)c.num_kv_heads * kv->max_seq * c.head_dim;
+    const size_t esz = kv->dtype == BT_KV_FP16 ? 2 : 4;
+    std::vector<uint8_t> hk(per * esz), hv(per * esz);
+    BT_CUDA_CHECK(cudaStreamSynchronize(e->stream));
+    BT_CUDA_CHECK(cudaMemcpy(hk.data(), static_cast<uint8_t*>(kv->k) + layer * per * esz, per * esz, cudaMemcpyDeviceToHost));
+    BT_CUDA_CHECK(cudaMemcpy(hv.data(), static_cast<uint8_t*>(kv->v) + layer * per * esz, per * esz, cudaMemcpyDeviceToHost));
+    const uint32_t H = c.num_kv_heads, hd = c.head_dim, S = kv->max_seq;
+    for (uint32_t h = 0; h < H; ++h)
+        for (uint32_t p = 0; p < S; ++p)
+            for (uint32_t d = 0; d < hd; ++d) {
+                const size_t src = ((size_t)h * S + p) * hd + d, dst = ((size_t)p * H + h) * hd + d;
+                if (esz == 2) {
+                    k[dst] = __half2float(reinterpret_cast<const __half*>(hk.data())[src]);
+                    v[dst] = __half2float(reinterpret_cast<const __half*>(hv.data())[src]);
+                } else {
+                    k[dst] = reinterpret_cast<const float*>(hk.data())[src];
+                    v[dst] = reinterpret_cast<const float*>(hv.data())[src];
+                }
+            }
+    return BT_OK;
+}
+
+int bt_engine_forward_token(bt_engine* e, bt_kv* kv, uint32_t token, uint32_t pos, float* logits, uint32_t* argmax) {
+    int rc = check_engine(e);
+    if (rc == BT_OK) rc = check_kv(e, kv);
+    if (rc != BT_OK) return rc;
+    if (token >= e->cfg.vocab_size) return fail(BT_ERR_OUT_OF_RANGE, "Token ID out of vocab bounds");
+    if (pos >= kv->max_seq) return fail(BT_ERR_OUT_OF_RANGE, "KVCache pos out of bounds");
+    DeviceGuard guard(e->device);
+    cudaStream_t s = e->stream;
+    DevState* h = kv->h_st;
+    std::memset(h, 0, sizeof(DevState));
+    h->pos = pos;
+    h->cur_token = token;
+    h->n_fixed = 0;
+    BT_CUDA_CHECK(cudaMemcpyAsync(kv->st, h, sizeof(DevState), cudaMemcpyHostToDevice, s));
+    kv->host_pos = pos;
+    rc = run_steps(e, kv, 1, s);
+    if (rc != BT_OK) return rc;
+    if (logits)
+        BT_CUDA_CHECK(cudaMemcpyAsync(logits, e->logits, sizeof(float) * e->cfg.vocab_size, cudaMemcpyDeviceToHost, s));
+    BT_CUDA_CHECK(cudaMemcpyAsync(h, kv->st, sizeof(DevState), cudaMemcpyDeviceToHost, s));
+    BT_CUDA_CHECK(cudaStreamSynchronize(s));
+    if (argmax) *argmax = h->last_argmax;
+    return BT_OK;
+}
+
+int bt_engine_begin(bt_engine* e, bt_kv* kv, const uint32_t* prompt, uint32_t n_prompt, uint32_t pos0) {
+    int rc = check_engine(e);
+    if (rc == BT_OK) rc = check_kv(e, kv);
+    if (rc != BT_OK) return rc;
+    if (!prompt || n_prompt == 0) return fail(BT_ERR_INVALID_ARGUMENT, "decode: empty prompt");
+    if ((uint64_t)pos0 + n_prompt > kv->max_seq) return fail(BT_ERR_OUT_OF_RANGE, "KVCache pos out of bounds");
+    for (uint32_t i = 0; i < n_prompt; ++i)
+        if (prompt[i] >= e->cfg.vocab_size) return fail(BT_ERR_OUT_OF_RANGE, "Token ID out of vocab bounds");
+    DeviceGuard guard(e->device);
+    cudaStream_t s = e->stream;
+    BT_CUDA_CHECK(cudaMemcpyAsync(kv->tok_hist + pos0, prompt, sizeof(uint32_t) * n_prompt, cudaMemcpyHostToDevice, s));
+    DevState* h = kv->h_st;
+    std::memset(h, 0, sizeof(DevState));
+    h->pos = pos0;
+    h->cur_token = prompt[0];
+    h->n_fixed = pos0 + n_prompt;
+    BT_CUDA_CHECK(cudaMemcpyAsync(kv->st, h, sizeof(DevState), cudaMemcpyHostToDevice, s));
+    BT_CUDA_CHECK(cudaStreamSynchronize(s));
+    kv->host_pos = pos0;
+    return ensure_graph(e, kv);
+}
+
+int bt_engine_steps(bt_engine* e, bt_kv* kv, uint32_t n, void* stream) {
+    int rc = check_engine(e);
+    if (rc == BT_OK) rc = check_kv(e, kv);
+    if (rc != BT_OK) return rc;
+    DeviceGuard guard(e->device);
+    return run_steps(e, kv, n, stream ? as_stream(stream) : e->stream);
+}
+
+int bt_engine_decode(bt_engine* e, bt_kv* kv, const uint32_t* prompt, uint32_t n_prompt, uint32_t pos0,
+                     uint32_t n_gen, uint32_t* tokens_out) {
+    if (!tokens_out) return fail(BT_ERR_INVALID_ARGUMENT, "decode: null tokens_out");
+    if (kv && (uint64_t)pos0 + n_prompt + n_gen > kv->max_seq)
+        return fail(BT_ERR_OUT_OF_RANGE, "KVCache pos out of bounds");
+    int rc = bt_engine_begin(e, kv, prompt, n_prompt, pos0);
+    if (rc != BT_OK) return rc;
+    DeviceGuard guard(e->device);
+    rc = run_steps(e, kv, n_prompt + n_gen, e->stream);
+    if (rc != BT_OK) return rc;
+    BT_CUDA_CHECK(cudaMemcpyAsync(tokens_out, kv->tok_hist + pos0, sizeof(uint32_t) * (n_prompt + n_gen + 1),
+                                  cudaMemcpyDeviceToHost, e->stream));
+    BT_CUDA_CHECK(cudaStreamSynchronize(e->stream));
+    return BT_OK;
+}
+
+int bt_engine_set_taps(bt_engine* e, int enable) {
+    if (!e) return fail(BT_ERR_INVALID_ARGUMENT, "null engine");
+    e->taps_on = enable != 0;
+    return BT_OK;
+}
+
+int bt_engine_read_taps(bt_engine* e, float* taps) {
+    if (!e || !taps) return fail(BT_ERR_INVALID_ARGUMENT, "null argument");
+    DeviceGuard guard(e->device);
+    BT_CUDA_CHECK(cudaStreamSynchronize(e->stream));
+    BT_CUDA_CHECK(cudaMemcpy(taps, e->taps, sizeof(float) * e->cfg.num_layers * e->cfg.dim, cudaMemcpyDeviceToHost));
+    return BT_OK;
+}
+
+int bt_kv_step_info(bt_kv* kv, uint32_t context, uint64_t* launches, uint64_t* bytes) {
+    if (!kv) return fail(BT_ERR_INVALID_ARGUMENT, "null KV cache");
+    const auto& c = kv->e->cfg;
+    const uint64_t D = c.dim, F = c.hidden_dim, KV = kvd(c), V = c.vocab_size, L = c.num_layers;
+    const uint64_t params = L * (D * D * 2 + KV * D * 2 + F * D * 3) + V * D;
+    const uint64_t weight_bytes = params + params / 32 * 4;
+    const uint64_t norms = 4 * D * (2 * L + 1);
+    const uint64_t emb = 4 * D;
+    const uint64_t esz = kv->dtype == BT_KV_FP16 ? 2 : 4;
+    const uint64_t kv_bytes = 2 * L * KV * esz * ((uint64_t)context + 1);  // read c positions, write 1
+    if (launches) *launches = 5 * L + 1;
+    if (bytes) *bytes = weight_bytes + norms + emb + kv_bytes;
+    return BT_OK;
+}
+
+int bt_kv_state(bt_kv* kv, uint32_t* pos, uint32_t* token, uint32_t* last_argmax) {
+    if (!kv) return fail(BT_ERR_INVALID_ARGUMENT, "null KV cache");
+    DeviceGuard guard(kv->e->device);
+    DevState h{};
+    BT_CUDA_CHECK(cudaStreamSynchronize(kv->e->stream));
+    BT_CUDA_CHECK(cudaMemcpy(&h, kv->st, sizeof(DevState), cudaMemcpyDeviceToHost));
+    if (pos) *pos = h.pos;
+    if (token) *token = h.cur_token;
+    if (last_argmax) *last_argmax = h.last_argmax;
+    return BT_OK;
+}
+
+void* bt_engine_stream(bt_engine* e) { return e ? (void*)e->stream : nullptr; }
+
+int bt_engine_profile(bt_engine* e, bt_kv* kv, uint32_t n_steps, float* ms_by_kind) {
+    int rc = check_engine(e);
+    if (rc == BT_OK) rc = check_kv(e, kv);
+    if (rc != BT_OK) return rc;
+    if (!ms_by_kind || n_steps == 0) return fail(BT_ERR_INVALID_ARGUMENT, "bt_engine_profile: bad argument");
+    if (kv->host_pos + n_steps > kv->max_seq) return fail(BT_ERR_OUT_OF_RANGE, "KVCache pos out of bounds");
+    DeviceGuard guard(e->device);
+    const int per_step = 5 * (int)e->cfg.num_layers + 1;
+    std::vector<cudaEvent_t> ev((size_t)per_step + 1);
+    for (auto& x : ev) BT_CUDA_CHECK(cudaEventCreate(&x));
+    for (int k = 0; k < 6; ++k) ms_by_kind[k] = 0.0f;
+    cudaStream_t s = e->stream;
+    for (uint32_t it = 0; it < n_steps && rc == BT_OK; ++it) {
+        Marks m{ev.data() + 1, 0};
+        cudaError_t ce = cudaEventRecord(ev[0], s);
+        if (ce != cudaSuccess) { rc = fail(BT_ERR_CUDA, cudaGetErrorString(ce)); break; }
+        g_launches.fetch_add((uint64_t)per_step, std::memory_order_relaxed);
+        rc = enqueue_step(e, kv, s, &m);
+        if (rc != BT_OK) break;
+        kv->host_pos += 1;
+        ce = cudaEventSynchronize(ev[per_step]);
+        if (ce != cudaSuccess) { rc = fail(BT_ERR_CUDA, cudaGetErrorString(ce)); break; }
+        for (int i = 0; i < per_step; ++i) {
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
+            const int kind = (i == per_step - 1) ? 5 : (i % 5);
+            ms_by_kind[kind] += ms;
+        }
+    }
+    for (auto& x : ev) cudaEventDestroy(x);
+    return rc;
+}
+
+}  // extern "C"

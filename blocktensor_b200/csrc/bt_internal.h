@@ -1,0 +1,32 @@
+// bt_internal.h -- host-side declarations shared between the .cu files.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace bt {
+
+// Row permutation applied while repacking a matrix into the device layout.
+struct RowMap {
+    int mode;          // 0 identity, 1 RoPE pair interleave within heads, 2 stride-2 interleave
+    uint32_t hd;       // head_dim for mode 1
+    uint32_t parity;   // 0/1 for mode 2
+    uint32_t src_off;  // row index of the first source row (slab offset)
+    uint32_t dst_off;  // added to the mapped row
+};
+
+// Launchers (stream-ordered, no synchronisation).  Return cudaError_t of the launch.
+cudaError_t launch_quantize_q8_0(const float* src, void* dst, uint64_t n_blocks, cudaStream_t s);
+cudaError_t launch_dequantize_q8_0(const void* src, float* dst, uint64_t n, cudaStream_t s);
+cudaError_t launch_repack_q8_0(const void* blocks, int8_t* qs, float* scales, uint32_t M, uint32_t K,
+                               RowMap map, cudaStream_t s);
+cudaError_t launch_gen_normal(uint64_t seed, uint64_t stream_id, uint64_t offset, uint64_t n, float k,
+                              float* out, cudaStream_t s);
+cudaError_t launch_fill(float* out, uint64_t n, float v, cudaStream_t s);
+
+// Same formula as the CPU oracle (oracle/bt_oracle.c bto_normal_k).
+float normal_k(float sigma);
+uint64_t splitmix64_host(uint64_t z);
+uint64_t stream_base_host(uint64_t seed, uint64_t stream);
+
+}  // namespace bt

@@ -1,0 +1,223 @@
+/*
+ * bt_cuda.h -- C ABI of the B200 (sm_100a) backend for BlockTensor's int8
+ * single-token decode path.
+ *
+ * Plain C: pointers, sizes and status codes only.  Device pointers are CUDA
+ * global-memory addresses on the current device; `stream` is a cudaStream_t
+ * passed as void* (NULL = legacy default stream).  Every entry point returns a
+ * status code (0 = success); bt_cuda_last_error() gives the message of the
+ * last failure on the calling thread.
+ *
+ * Status codes mirror the exceptions of the reference so that a C++ wrapper
+ * can rethrow the same types:
+ *   BT_ERR_OUT_OF_RANGE      std::out_of_range     (token >= vocab,
+ *                            runtime/src/transformer_engine.cpp:229-231;
+ *                            pos >= max_seq, runtime/src/kv_cache.cpp:18-19)
+ *   BT_ERR_RUNTIME           std::runtime_error    (I/O, bad magic,
+ *                            models/model_importer.cpp:12,46,50)
+ *   BT_ERR_INVALID_ARGUMENT  std::invalid_argument (n % 32 != 0,
+ *                            quantization/quant_types.cpp:9-11; null buffers,
+ *                            memory/memory_manager.cpp:10,29,52)
+ */
+#ifndef BT_CUDA_H
+#define BT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define BT_API __attribute__((visibility("default")))
+#else
+#define BT_API
+#endif
+
+#define BT_OK                    0
+#define BT_ERR_UNKNOWN          -1
+#define BT_ERR_OUT_OF_RANGE     -2
+#define BT_ERR_RUNTIME          -3
+#define BT_ERR_INVALID_ARGUMENT -4
+#define BT_ERR_CUDA             -5
+#define BT_ERR_OUT_OF_MEMORY    -6
+#define BT_ERR_DEVICE_TIMEOUT   -7
+
+#define BT_ABI_VERSION 1
+
+/* KV-cache element types. */
+#define BT_KV_FP32 0
+#define BT_KV_FP16 1
+
+/* Layout and field order of blocktensor::ModelConfig
+ * (runtime/include/blocktensor/model_config.hpp:9-19); 36 bytes, so a
+ * .btmodel header (models/model_importer.cpp:15,53) can be passed as-is. */
+typedef struct bt_model_config {
+    uint32_t vocab_size;
+    uint32_t dim;
+    uint32_t hidden_dim;
+    uint32_t num_layers;
+    uint32_t num_heads;
+    uint32_t num_kv_heads;
+    uint32_t head_dim;
+    uint32_t max_seq_len;
+    float    rms_norm_eps;
+} bt_model_config;
+
+/* Engine options that the reference hard-codes. */
+typedef struct bt_engine_options {
+    float    rope_theta;   /* 10000.0f in kernels/cpu_ref.hpp:40; 500000 for Llama-3 shapes */
+    uint32_t reserved[7];
+} bt_engine_options;
+
+/* One tensor of a model, as the .btmodel file stores it
+ * (models/model_importer.cpp:27-41): fp32 for embeddings and norms, an array
+ * of 36-byte BlockQ8_0 {float scale; int8 qs[32]} (quantization/quant_types.hpp:12-15)
+ * for every projection matrix. */
+typedef struct bt_tensor_view {
+    const void* data;
+    uint64_t    bytes;
+} bt_tensor_view;
+
+typedef struct bt_engine bt_engine;
+typedef struct bt_kv bt_kv;
+
+/* ------------------------------------------------------------------ */
+/* Library                                                              */
+/* ------------------------------------------------------------------ */
+BT_API int         bt_cuda_abi_version(void);
+BT_API const char* bt_cuda_last_error(void);
+/* Number of kernel launches this library has issued on the calling process. */
+BT_API uint64_t    bt_cuda_launch_count(void);
+
+/* ------------------------------------------------------------------ */
+/* Quantization on device (quantization/quant_types.cpp)               */
+/* ------------------------------------------------------------------ */
+
+/* Replaces quantization::quantize_q8_0 (quant_types.cpp:8-34, decl.
+ * quant_types.hpp:22).  src: n fp32; dst: n/32 BlockQ8_0 (36 B each).
+ * Bit-exact with the reference for finite inputs.  n % 32 != 0 ->
+ * BT_ERR_INVALID_ARGUMENT. */
+BT_API int bt_cuda_quantize_q8_0(const float* src, void* dst_blocks, uint64_t n, void* stream);
+
+/* Replaces quantization::dequantize_q8_0 (quant_types.cpp:36-48, decl. quant_types.hpp:23). */
+BT_API int bt_cuda_dequantize_q8_0(const void* src_blocks, float* dst, uint64_t n, void* stream);
+
+/* Replaces quantization::matvec_q8_0 (quant_types.cpp:101-121, decl.
+ * quant_types.hpp:28) and the "matvec_q8_0" pipeline of the Vulkan backend
+ * (kernels/glsl/matvec_q8_0.comp, bound at transformer_engine.cpp:76-77):
+ * Y[M] = W[M x N] X[N] with W in the reference's 36-byte block layout. */
+BT_API int bt_cuda_matvec_q8_0(const void* W_blocks, const float* X, float* Y,
+                        uint32_t M, uint32_t N, void* stream);
+
+/* Split reference blocks into the device layout: qs[M][K] int8 (rows 16-byte
+ * aligned) and scales[M][K/32] fp32.  No reference counterpart (the reference
+ * keeps the 36-byte blocks); this is the upload repack of
+ * MemoryManager::copy_host_to_device (memory/memory_manager.cpp:22-42). */
+BT_API int bt_cuda_repack_q8_0(const void* W_blocks, int8_t* qs, float* scales,
+                        uint32_t M, uint32_t K, void* stream);
+
+/* Batched int8 GEMV on the device layout: Y[b][m] = sum_k W[m][k] X[b][k],
+ * b < B, for the dequant-GEMV microbenchmark.  B = 1 is the
+ * reference's matvec_q8_0 (quant_types.cpp:101-121) on repacked weights. */
+BT_API int bt_cuda_gemv_q8(const int8_t* qs, const float* scales, const float* X, float* Y,
+                    uint32_t M, uint32_t K, uint32_t B, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Math primitives (kernels/cpu_ref.hpp, sampler.hpp) on device         */
+/* ------------------------------------------------------------------ */
+/* cpu_ref::rmsnorm (cpu_ref.hpp:11-28); pipeline "rmsnorm", push {dim, eps}. */
+BT_API int bt_cuda_rmsnorm(const float* in, const float* w, float* out, uint32_t rows, uint32_t dim,
+                    float eps, void* stream);
+/* cpu_ref::rope (cpu_ref.hpp:30-53) with the base as a parameter; pipeline "rope". */
+BT_API int bt_cuda_rope(const float* in, float* out, uint32_t seq, uint32_t heads, uint32_t head_dim,
+                 uint32_t pos, float theta, void* stream);
+/* cpu_ref::softmax (cpu_ref.hpp:55-72); pipeline "softmax". */
+BT_API int bt_cuda_softmax(const float* in, float* out, uint32_t rows, uint32_t dim, void* stream);
+/* cpu_ref::silu (cpu_ref.hpp:74-79); pipeline "silu". */
+BT_API int bt_cuda_silu(const float* in, float* out, uint32_t n, void* stream);
+/* sampling::sample_greedy (sampler.hpp:11-13): first maximum wins. out: device uint32. */
+BT_API int bt_cuda_argmax(const float* logits, uint32_t n, uint32_t* out, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Engine (runtime/include/blocktensor/transformer_engine.hpp:12-56)    */
+/* ------------------------------------------------------------------ */
+
+/* Replaces TransformerEngine::TransformerEngine(backend, weights)
+ * (transformer_engine.hpp:14): creates the device context and allocates
+ * device-resident weights for `cfg` on CUDA device `device`.  opt may be NULL
+ * (rope_theta 10000).  Weights are loaded next by bt_engine_load or
+ * bt_engine_generate. */
+BT_API int bt_engine_create(int device, const bt_model_config* cfg, const bt_engine_options* opt,
+                     bt_engine** out);
+BT_API int bt_engine_destroy(bt_engine* e);
+
+/* Loads the 3 + 9*num_layers tensors of a model in .btmodel order
+ * (models/model_importer.cpp:69-85: embed, out_norm, head, then per layer
+ * attn_norm, ffn_norm, q, k, v, o, gate, up, down).  on_device = 0: host
+ * pointers (importer output, IComputeBuffer::map of HOST_VISIBLE buffers);
+ * on_device = 1: device pointers.  Matrices are repacked on the device. */
+BT_API int bt_engine_load(bt_engine* e, const bt_tensor_view* tensors, uint32_t n_tensors, int on_device);
+
+/* Seeded synthetic weights generated on the device: matrices
+ * approximately N(0, sigma) (sum of four 16-bit uniforms), quantized with the
+ * device quantizer; embeddings N(0, sigma) fp32; norms 1.0.  Bit-identical to
+ * the CPU oracle's generator for the same seed. */
+BT_API int bt_engine_generate(bt_engine* e, uint64_t seed, float sigma);
+
+/* Replaces KVCache(MemoryManager&, num_layers, max_seq_len, kv_heads, head_dim)
+ * (runtime/include/blocktensor/kv_cache.hpp:12): device-resident cache of
+ * max_seq positions in fp32 (BT_KV_FP32) or fp16 (BT_KV_FP16). */
+BT_API int bt_kv_create(bt_engine* e, uint32_t max_seq, int kv_dtype, bt_kv** out);
+BT_API int bt_kv_destroy(bt_kv* kv);
+/* Reads one layer in the reference layout [max_seq][kv_heads][head_dim] as fp32
+ * (runtime/src/kv_cache.cpp:21-23).  k, v: host, max_seq*kv_heads*head_dim floats. */
+BT_API int bt_kv_read_layer(bt_kv* kv, uint32_t layer, float* k, float* v);
+
+/* Replaces TransformerEngine::forward_single_token(token, pos, KVCache&)
+ * (transformer_engine.hpp:17, transformer_engine.cpp:228-251): one decode
+ * step.  logits: host [vocab] or NULL; argmax: host or NULL (greedy token,
+ * sampler.hpp:11-13).  token >= vocab or pos >= max_seq -> BT_ERR_OUT_OF_RANGE. */
+BT_API int bt_engine_forward_token(bt_engine* e, bt_kv* kv, uint32_t token, uint32_t pos,
+                            float* logits, uint32_t* argmax);
+
+/* The prompt-then-greedy loop of bt_infer/bench_runner
+ * (tools/bt_infer.cpp:116-136, benchmarks/bench_runner.cpp:105-119) on the
+ * device: positions pos0 .. pos0+n_prompt+n_gen-1, the step at position p
+ * consuming prompt[p-pos0] while p-pos0 < n_prompt and the previous step's
+ * argmax afterwards.  tokens_out (host, n_prompt + n_gen + 1 entries) gets the
+ * token consumed at each position plus the final argmax.  No host round trip
+ * between steps. */
+BT_API int bt_engine_decode(bt_engine* e, bt_kv* kv, const uint32_t* prompt, uint32_t n_prompt,
+                     uint32_t pos0, uint32_t n_gen, uint32_t* tokens_out);
+
+/* Per-layer residual-stream taps: when enabled, every subsequent step records
+ * x after each layer; bt_engine_read_taps copies [num_layers][dim] fp32 of the
+ * last step to host. */
+BT_API int bt_engine_set_taps(bt_engine* e, int enable);
+BT_API int bt_engine_read_taps(bt_engine* e, float* taps);
+
+/* Device-side timing hooks for benchmarks: run n decode steps on `stream`
+ * with no host synchronisation; the device state (position, current token)
+ * continues from the last call. */
+BT_API int bt_engine_begin(bt_engine* e, bt_kv* kv, const uint32_t* prompt, uint32_t n_prompt, uint32_t pos0);
+BT_API int bt_engine_steps(bt_engine* e, bt_kv* kv, uint32_t n, void* stream);
+/* The engine's own stream (cudaStream_t), on which every call above runs. */
+BT_API void* bt_engine_stream(bt_engine* e);
+/* Per-kernel timing: runs n_steps decode steps eagerly (no graph, no
+ * overlap between kernels) with a CUDA event after every launch and adds the
+ * device time of each kernel kind into ms_by_kind[6] = {qkv, attention,
+ * o-proj, gate/up, down, head}.  Advances the sequence like bt_engine_steps. */
+BT_API int bt_engine_profile(bt_engine* e, bt_kv* kv, uint32_t n_steps, float* ms_by_kind);
+/* Position, current token and last argmax of the sequence (host copy). */
+BT_API int bt_kv_state(bt_kv* kv, uint32_t* pos, uint32_t* token, uint32_t* last_argmax);
+/* Kernel launches of one decode step and the algorithmic HBM bytes it moves
+ * when the step processes position context-1: weights (int8 + fp32 scales),
+ * norms, one embedding row, KV read of `context` positions and the KV write. */
+BT_API int bt_kv_step_info(bt_kv* kv, uint32_t context, uint64_t* launches, uint64_t* bytes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BT_CUDA_H */
