@@ -190,6 +190,9 @@ def run_ours(args):
     prompt_len, W, K = args.prompt, args.warmup, args.steps
     max_seq = prompt_len + W + K + args.e2e_steps + args.profile_steps + 2
     cfg = synthetic.config(shape, max_seq)
+    if args.layers:
+        # truncated depth, for small profiler captures only (never a bench line)
+        cfg.num_layers = args.layers
     t0 = time.time()
     eng = bt.TransformerEngine(cfg, device=local, rope_theta=synthetic.ROPE_THETA[shape])
     eng.generate(seed=0, sigma=0.02)
@@ -295,7 +298,8 @@ def run_ours(args):
                        "global_batch": world, "seq_len": prompt_len, "prompt": prompt_len, "decode_steps": K,
                        "kv_cache": "fp16", "activations": "fp32", "weights": "int8 Q8_0 (fp32 scale per 32)",
                        "parallelism": f"replicas{world}" if world > 1 else "single",
-                       "l2": "inputs larger than L2 (7.4 GB of weights per step)"},
+                       "l2": "inputs larger than L2 (7.4 GB of weights per step)",
+                       "truncated_layers": args.layers or None},
             "roofline": {"kernel": "decode_step", "bound": "hbm", "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
                          "bytes_per_step": bytes_avg, "traffic": traffic,
@@ -332,6 +336,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--profile-steps", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="truncate the model to N layers (profiler captures; the JSON line is then marked)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

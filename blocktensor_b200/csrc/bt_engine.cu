@@ -16,6 +16,7 @@
 // (:233-238) instead of copying the whole table to the host.
 #include "bt_common.cuh"
 #include "bt_gemv.cuh"
+#include "bt_gemv_stream.cuh"
 #include "bt_internal.h"
 
 #include <cmath>
@@ -70,26 +71,35 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnArgs a) {
     const KVT* kb = reinterpret_cast<const KVT*>(a.k) + (size_t)kvh * a.max_seq * HD;
     const KVT* vb = reinterpret_cast<const KVT*>(a.v) + (size_t)kvh * a.max_seq * HD;
 
-    // scores: one warp per key, lanes over head dims
-    for (uint32_t t = warp; t < nk; t += nw) {
-        const KVT* kr = kb + (size_t)(t0 + t) * HD;
-        float kv[NV];
+    // scores: one warp per key, lanes over head dims; 4 keys per warp in flight
+    constexpr int KU = 4;
+    for (uint32_t tb = warp; tb < nk; tb += KU * nw) {
+        float kv[KU][NV];
 #pragma unroll
-        for (int i = 0; i < NV; ++i) {
-            const uint32_t d = lane + 32 * i;
-            kv[i] = d < HD ? KVConv<KVT>::to_f(kr[d]) : 0.0f;
-        }
-#pragma unroll
-        for (uint32_t g = 0; g < GT; ++g) {
-            if (g >= G) break;
-            float p = 0.0f;
+        for (int u = 0; u < KU; ++u) {
+            const uint32_t t = tb + u * nw;
+            const KVT* kr = kb + (size_t)(t0 + (t < nk ? t : 0)) * HD;
 #pragma unroll
             for (int i = 0; i < NV; ++i) {
                 const uint32_t d = lane + 32 * i;
-                if (d < HD) p = fmaf(qs[g * HD + d], kv[i], p);
+                kv[u][i] = (t < nk && d < HD) ? KVConv<KVT>::to_f(kr[d]) : 0.0f;
             }
-            p = warp_sum(p);
-            if (lane == 0) sc[g * a.lmax + t] = __fmul_rn(p, a.scale);
+        }
+#pragma unroll
+        for (int u = 0; u < KU; ++u) {
+            const uint32_t t = tb + u * nw;
+#pragma unroll
+            for (uint32_t g = 0; g < GT; ++g) {
+                if (g >= G) break;
+                float p = 0.0f;
+#pragma unroll
+                for (int i = 0; i < NV; ++i) {
+                    const uint32_t d = lane + 32 * i;
+                    if (d < HD) p = fmaf(qs[g * HD + d], kv[u][i], p);
+                }
+                p = warp_sum(p);
+                if (lane == 0 && t < nk) sc[g * a.lmax + t] = __fmul_rn(p, a.scale);
+            }
         }
     }
     __syncthreads();
@@ -114,7 +124,18 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnArgs a) {
         float acc[GT];
 #pragma unroll
         for (int g = 0; g < GT; ++g) acc[g] = 0.0f;
-        for (uint32_t t = 0; t < nk; ++t) {
+        uint32_t t = 0;
+        for (; t + 8 <= nk; t += 8) {  // 8 V rows in flight per thread
+            float vv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) vv[u] = KVConv<KVT>::to_f(vb[(size_t)(t0 + t + u) * HD + d]);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+#pragma unroll
+                for (int g = 0; g < GT; ++g)
+                    if ((uint32_t)g < G) acc[g] = fmaf(sc[g * a.lmax + t + u], vv[u], acc[g]);
+        }
+        for (; t < nk; ++t) {
             const float vv = KVConv<KVT>::to_f(vb[(size_t)(t0 + t) * HD + d]);
 #pragma unroll
             for (int g = 0; g < GT; ++g)
@@ -211,6 +232,8 @@ struct bt_engine {
     cudaStream_t stream = nullptr;
     bool pdl = true;
     bool use_graph = true;
+    bool use_stream = true;   // bulk-copy streaming GEMV where the shape allows
+    uint32_t num_sms = 148;
     bool taps_on = false;
     std::vector<void*> allocs;
     std::vector<LayerDev> layers;
@@ -392,6 +415,9 @@ int enqueue_step(bt_engine* e, bt_kv* kv, cudaStream_t s, Marks* marks = nullptr
     const uint32_t D = c.dim, F = c.hidden_dim, KV = kvd(c), hd = c.head_dim;
     const uint32_t G = c.num_heads / c.num_kv_heads;
     const bool pdl = e->pdl && !marks;
+    const bool stream = e->use_stream;
+    const uint32_t nsm = e->num_sms;
+    uint32_t* errp = &kv->st->error;
     const size_t kv_layer = (size_t)c.num_kv_heads * kv->max_seq * hd;
     const size_t esz = kv->dtype == BT_KV_FP16 ? 2 : 4;
     const float scale = 1.0f / std::sqrt((float)hd);
@@ -403,15 +429,16 @@ int enqueue_step(bt_engine* e, bt_kv* kv, cudaStream_t s, Marks* marks = nullptr
         {
             GemvW g{L.qkv_q, L.qkv_s, D + 2 * KV, D};
             ProNorm pro{e->x, L.attn_norm, c.rms_norm_eps, l == 0 ? e->embed : nullptr, kv->st, e->x};
+            SProNorm spro{e->x, L.attn_norm, c.rms_norm_eps, l == 0 ? e->embed : nullptr, kv->st, e->x};
             cudaError_t err;
             if (kv->dtype == BT_KV_FP16) {
                 EpiQKV<__half> epi{e->q, reinterpret_cast<__half*>(kl), reinterpret_cast<__half*>(vl), kv->rope, kv->st,
                                    D, KV, hd, kv->max_seq};
-                err = launch_gemv(g, pro, epi, s, pdl, 4);
+                err = launch_gemv_best(g, spro, SEpiQKV<__half>{epi}, pro, epi, true, errp, nsm, s, pdl, stream);
             } else {
                 EpiQKV<float> epi{e->q, reinterpret_cast<float*>(kl), reinterpret_cast<float*>(vl), kv->rope, kv->st,
                                   D, KV, hd, kv->max_seq};
-                err = launch_gemv(g, pro, epi, s, pdl, 4);
+                err = launch_gemv_best(g, spro, SEpiQKV<float>{epi}, pro, epi, true, errp, nsm, s, pdl, stream);
             }
             BT_CUDA_CHECK(err);
             BT_MARK();
@@ -426,24 +453,36 @@ int enqueue_step(bt_engine* e, bt_kv* kv, cudaStream_t s, Marks* marks = nullptr
             BT_MARK();
         }
         // o-proj + residual
-        BT_CUDA_CHECK(launch_gemv(GemvW{L.o_q, L.o_s, D, D}, ProCopy{e->attn}, EpiResidual{e->x, nullptr}, s, pdl));
-        BT_MARK();
+        {
+            EpiResidual epi{e->x, nullptr};
+            BT_CUDA_CHECK(launch_gemv_best(GemvW{L.o_q, L.o_s, D, D}, SProCopy{e->attn}, SEpiResidual{e->x, nullptr},
+                                           ProCopy{e->attn}, epi, false, errp, nsm, s, pdl, stream));
+            BT_MARK();
+        }
         // gate/up + SwiGLU
-        BT_CUDA_CHECK(launch_gemv(GemvW{L.gu_q, L.gu_s, 2 * F, D},
-                                  ProNorm{e->x, L.ffn_norm, c.rms_norm_eps, nullptr, nullptr, nullptr},
-                                  EpiSwiGLU{e->act}, s, pdl, 4));
-        BT_MARK();
+        {
+            ProNorm pro{e->x, L.ffn_norm, c.rms_norm_eps, nullptr, nullptr, nullptr};
+            SProNorm spro{e->x, L.ffn_norm, c.rms_norm_eps, nullptr, nullptr, nullptr};
+            BT_CUDA_CHECK(launch_gemv_best(GemvW{L.gu_q, L.gu_s, 2 * F, D}, spro, SEpiSwiGLU{e->act}, pro,
+                                           EpiSwiGLU{e->act}, true, errp, nsm, s, pdl, stream));
+            BT_MARK();
+        }
         // down + residual (+ tap)
-        BT_CUDA_CHECK(launch_gemv(GemvW{L.d_q, L.d_s, D, F}, ProCopy{e->act},
-                                  EpiResidual{e->x, e->taps_on ? e->taps + (size_t)l * D : nullptr}, s, pdl));
+        {
+            float* tap = e->taps_on ? e->taps + (size_t)l * D : nullptr;
+            BT_CUDA_CHECK(launch_gemv_best(GemvW{L.d_q, L.d_s, D, F}, SProCopy{e->act}, SEpiResidual{e->x, tap},
+                                           ProCopy{e->act}, EpiResidual{e->x, tap}, false, errp, nsm, s, pdl, stream));
+            BT_MARK();
+        }
+    }
+    {
+        ProNorm pro{e->x, e->out_norm, c.rms_norm_eps, nullptr, nullptr, nullptr};
+        SProNorm spro{e->x, e->out_norm, c.rms_norm_eps, nullptr, nullptr, nullptr};
+        EpiLogits epi{e->logits, e->am_val, e->am_idx, e->am_ticket, kv->st, kv->tok_hist, kv->max_seq};
+        BT_CUDA_CHECK(launch_gemv_best(GemvW{e->head_q, e->head_s, c.vocab_size, D}, spro, SEpiLogits{epi}, pro, epi,
+                                       false, errp, nsm, s, pdl, stream));
         BT_MARK();
     }
-    BT_CUDA_CHECK(launch_gemv(GemvW{e->head_q, e->head_s, c.vocab_size, D},
-                              ProNorm{e->x, e->out_norm, c.rms_norm_eps, nullptr, nullptr, nullptr},
-                              EpiLogits{e->logits, e->am_val, e->am_idx, e->am_ticket, kv->st, kv->tok_hist,
-                                        kv->max_seq},
-                              s, pdl));
-    BT_MARK();
     return BT_OK;
 }
 
@@ -523,6 +562,10 @@ int bt_engine_create(int device, const bt_model_config* cfg, const bt_engine_opt
     if (opt && opt->rope_theta > 0.0f) e->theta = opt->rope_theta;
     if (const char* v = std::getenv("BT_NO_PDL")) e->pdl = (v[0] == '0');
     if (const char* v = std::getenv("BT_NO_GRAPH")) e->use_graph = (v[0] == '0');
+    if (const char* v = std::getenv("BT_NO_STREAM")) e->use_stream = (v[0] == '0');
+    int nsm = 0;
+    BT_CUDA_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device));
+    e->num_sms = nsm > 0 ? (uint32_t)nsm : 148;
     BT_CUDA_CHECK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     rc = alloc_weights(e.get());
     if (rc != BT_OK) {
@@ -789,6 +832,7 @@ int bt_engine_forward_token(bt_engine* e, bt_kv* kv, uint32_t token, uint32_t po
         BT_CUDA_CHECK(cudaMemcpyAsync(logits, e->logits, sizeof(float) * e->cfg.vocab_size, cudaMemcpyDeviceToHost, s));
     BT_CUDA_CHECK(cudaMemcpyAsync(h, kv->st, sizeof(DevState), cudaMemcpyDeviceToHost, s));
     BT_CUDA_CHECK(cudaStreamSynchronize(s));
+    if (h->error) return fail(BT_ERR_DEVICE_TIMEOUT, "device wait timed out during the decode step");
     if (argmax) *argmax = h->last_argmax;
     return BT_OK;
 }
@@ -835,7 +879,9 @@ int bt_engine_decode(bt_engine* e, bt_kv* kv, const uint32_t* prompt, uint32_t n
     if (rc != BT_OK) return rc;
     BT_CUDA_CHECK(cudaMemcpyAsync(tokens_out, kv->tok_hist + pos0, sizeof(uint32_t) * (n_prompt + n_gen + 1),
                                   cudaMemcpyDeviceToHost, e->stream));
+    BT_CUDA_CHECK(cudaMemcpyAsync(kv->h_st, kv->st, sizeof(DevState), cudaMemcpyDeviceToHost, e->stream));
     BT_CUDA_CHECK(cudaStreamSynchronize(e->stream));
+    if (kv->h_st->error) return fail(BT_ERR_DEVICE_TIMEOUT, "device wait timed out during decode");
     return BT_OK;
 }
 

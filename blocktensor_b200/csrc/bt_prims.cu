@@ -6,6 +6,7 @@
 // kernel-level parity tests.
 #include "bt_common.cuh"
 #include "bt_gemv.cuh"
+#include "bt_gemv_stream.cuh"
 #include "bt_internal.h"
 
 namespace bt {
@@ -204,6 +205,60 @@ using namespace bt;
 
 extern "C" {
 
+int bt_cuda_device_info(int device, char* name, uint64_t* total_bytes, uint32_t* max_threads_per_block,
+                        uint32_t* max_shared_bytes) {
+    cudaDeviceProp p;
+    BT_CUDA_CHECK(cudaGetDeviceProperties(&p, device));
+    if (name) {
+        snprintf(name, 256, "%s", p.name);
+    }
+    if (total_bytes) *total_bytes = p.totalGlobalMem;
+    if (max_threads_per_block) *max_threads_per_block = (uint32_t)p.maxThreadsPerBlock;
+    if (max_shared_bytes) *max_shared_bytes = (uint32_t)p.sharedMemPerBlockOptin;
+    return BT_OK;
+}
+
+int bt_cuda_alloc(int device, uint64_t bytes, void** ptr) {
+    BT_CHECK_ARG(ptr, "alloc: null output");
+    BT_CUDA_CHECK(cudaSetDevice(device));
+    void* p = nullptr;
+    BT_CUDA_CHECK(cudaMalloc(&p, bytes ? bytes : 16));
+    cudaError_t e = cudaMemset(p, 0, bytes ? bytes : 16);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return fail(BT_ERR_CUDA, cudaGetErrorString(e));
+    }
+    *ptr = p;
+    return BT_OK;
+}
+
+int bt_cuda_free(int device, void* ptr) {
+    if (!ptr) return BT_OK;
+    BT_CUDA_CHECK(cudaSetDevice(device));
+    BT_CUDA_CHECK(cudaFree(ptr));
+    return BT_OK;
+}
+
+int bt_cuda_copy_h2d(int device, void* dst, const void* src, uint64_t bytes) {
+    BT_CHECK_ARG(bytes == 0 || (dst && src), "copy_h2d: null buffer");
+    BT_CUDA_CHECK(cudaSetDevice(device));
+    BT_CUDA_CHECK(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+    return BT_OK;
+}
+
+int bt_cuda_copy_d2h(int device, void* dst, const void* src, uint64_t bytes) {
+    BT_CHECK_ARG(bytes == 0 || (dst && src), "copy_d2h: null buffer");
+    BT_CUDA_CHECK(cudaSetDevice(device));
+    BT_CUDA_CHECK(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost));
+    return BT_OK;
+}
+
+int bt_cuda_synchronize(int device) {
+    BT_CUDA_CHECK(cudaSetDevice(device));
+    BT_CUDA_CHECK(cudaDeviceSynchronize());
+    return BT_OK;
+}
+
 int bt_cuda_rmsnorm(const float* in, const float* w, float* out, uint32_t rows, uint32_t dim, float eps,
                     void* stream) {
     BT_CHECK_ARG(in && w && out, "rmsnorm: null buffer");
@@ -276,7 +331,16 @@ int bt_cuda_gemv_q8(const int8_t* qs, const float* scales, const float* X, float
     if (M == 0) return BT_OK;
     cudaStream_t s = as_stream(stream);
     cudaError_t e;
-    if (B == 1) e = launch_gemv(GemvW{qs, scales, M, K}, ProCopy{X}, EpiStore{Y}, s, false);
+    if (B == 1) {
+        static int nsm_cache[64] = {};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev < 0 || dev >= 64) dev = 0;
+        if (!nsm_cache[dev]) cudaDeviceGetAttribute(&nsm_cache[dev], cudaDevAttrMultiProcessorCount, dev);
+        const GemvW g{qs, scales, M, K};
+        e = launch_gemv_best(g, SProCopy{X}, SEpiStore{Y}, ProCopy{X}, EpiStore{Y}, false, nullptr,
+                             (uint32_t)nsm_cache[dev], s, false, true);
+    }
     else if (B == 2) e = launch_gemv_batch<2>(qs, scales, X, Y, M, K, B, s);
     else if (B <= 4) e = launch_gemv_batch<4>(qs, scales, X, Y, M, K, B, s);
     else if (B <= 8) e = launch_gemv_batch<8>(qs, scales, X, Y, M, K, B, s);

@@ -69,6 +69,12 @@ SIGNATURES = {
     "bt_cuda_abi_version": (_i32, []),
     "bt_cuda_last_error": (C.c_char_p, []),
     "bt_cuda_launch_count": (_u64, []),
+    "bt_cuda_device_info": (_i32, [_i32, C.c_char_p, _vp, _vp, _vp]),
+    "bt_cuda_alloc": (_i32, [_i32, _u64, C.POINTER(_vp)]),
+    "bt_cuda_free": (_i32, [_i32, _vp]),
+    "bt_cuda_copy_h2d": (_i32, [_i32, _vp, _vp, _u64]),
+    "bt_cuda_copy_d2h": (_i32, [_i32, _vp, _vp, _u64]),
+    "bt_cuda_synchronize": (_i32, [_i32]),
     "bt_cuda_quantize_q8_0": (_i32, [_vp, _vp, _u64, _vp]),
     "bt_cuda_dequantize_q8_0": (_i32, [_vp, _vp, _u64, _vp]),
     "bt_cuda_matvec_q8_0": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp]),

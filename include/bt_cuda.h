@@ -92,6 +92,23 @@ BT_API const char* bt_cuda_last_error(void);
 BT_API uint64_t    bt_cuda_launch_count(void);
 
 /* ------------------------------------------------------------------ */
+/* Device memory for IComputeBuffer implementations                     */
+/* (runtime/include/blocktensor/backend.hpp:32-43, memory/memory_manager.cpp) */
+/* ------------------------------------------------------------------ */
+/* Device name, total memory and the limits that DeviceInfo
+ * (backend.hpp:56-66) reports. name: at least 256 bytes. */
+BT_API int bt_cuda_device_info(int device, char* name, uint64_t* total_bytes, uint32_t* max_threads_per_block,
+                               uint32_t* max_shared_bytes);
+/* Allocates `bytes` (zero-filled) on `device`. */
+BT_API int bt_cuda_alloc(int device, uint64_t bytes, void** ptr);
+BT_API int bt_cuda_free(int device, void* ptr);
+/* Synchronous copies (IComputeBuffer::write / read). */
+BT_API int bt_cuda_copy_h2d(int device, void* dst, const void* src, uint64_t bytes);
+BT_API int bt_cuda_copy_d2h(int device, void* dst, const void* src, uint64_t bytes);
+/* IComputeBackend::synchronize (backend.hpp:91). */
+BT_API int bt_cuda_synchronize(int device);
+
+/* ------------------------------------------------------------------ */
 /* Quantization on device (quantization/quant_types.cpp)               */
 /* ------------------------------------------------------------------ */
 
