@@ -101,6 +101,27 @@ def repack_q8_0(blocks, M: int, K: int, stream=None):
     return qs, sc
 
 
+def unit_bytes(M: int, K: int) -> int:
+    """Bytes of an M x K matrix in the tensor-core unit layout."""
+    return (M + 15) // 16 * (K // Q8_BLOCK) * 576
+
+
+def pack_q8_units(blocks, M: int, K: int, stream=None):
+    """36-byte blocks -> the unit layout of the tensor-core GEMV (uint8 CUDA tensor)."""
+    torch = _torch()
+    units = torch.empty(unit_bytes(M, K), dtype=torch.uint8, device=blocks.device)
+    call("bt_cuda_pack_q8_units", _dev_ptr(blocks), _dev_ptr(units), M, K, _stream(stream))
+    return units
+
+
+def gemv_q8_units(units, x, M: int, K: int, stream=None, out=None):
+    """y = W x on the unit layout (tensor-core GEMV of the decode engine)."""
+    torch = _torch()
+    y = out if out is not None else torch.empty(M, dtype=torch.float32, device=x.device)
+    call("bt_cuda_gemv_q8_units", _dev_ptr(units), _dev_ptr(x), _dev_ptr(y), M, K, _stream(stream))
+    return y
+
+
 def gemv_q8(qs, scales, x, stream=None, out=None):
     """y[b] = W x[b] for x of shape [B, K] (B <= 16), W in the device layout."""
     torch = _torch()

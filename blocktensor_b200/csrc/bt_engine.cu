@@ -16,7 +16,8 @@
 // (:233-238) instead of copying the whole table to the host.
 #include "bt_common.cuh"
 #include "bt_gemv.cuh"
-#include "bt_gemv_stream.cuh"
+#include "bt_gemv_mma.cuh"
+#include "bt_attention.cuh"
 #include "bt_internal.h"
 
 #include <cmath>
@@ -28,199 +29,18 @@
 
 namespace bt {
 
-// ---------------------------------------------------------------- attention
-
-struct AttnArgs {
-    const float* q;       // [H][hd] (after RoPE)
-    const void* k;        // layer base [KVH][max_seq][hd]
-    const void* v;
-    float* out;           // [H][hd]
-    float* part;          // [H][S][hd + 2]: m, l, o[hd]
-    uint32_t* ticket;     // [KVH]
-    const DevState* st;
-    uint32_t hd, G, max_seq, lmax;
-    float scale;          // 1/sqrt(hd) (transformer_engine.cpp:158)
-};
-
-// Grid (KVH, S): CTA (kvh, s) handles the G query heads of kv head kvh
-// (GQA map h / (H/KVH), transformer_engine.cpp:161) over keys
-// [s*L, min(c, (s+1)*L)), L = ceil(c/S), c = pos + 1.  It writes an
-// unnormalised partial (max m, sum l, o = sum e^(s-m) v); the last CTA of a
-// KV head (atomic ticket) merges the S partials.
-template <int NV, int GT, typename KVT>
-__global__ void __launch_bounds__(128) attn_decode_kernel(AttnArgs a) {
-    extern __shared__ float sm[];
-    __shared__ float s_m[16], s_l[16];
-    __shared__ bool s_last;
-    pdl_trigger();
-    pdl_wait();
-    const uint32_t kvh = blockIdx.x, sidx = blockIdx.y, S = gridDim.y;
-    const uint32_t HD = a.hd, G = a.G;
-    const uint32_t c = min(a.st->pos + 1, a.max_seq);
-    const uint32_t L = (c + S - 1) / S;
-    const uint32_t t0 = sidx * L;
-    const uint32_t t1 = min(c, t0 + L);
-    const uint32_t nk = t1 > t0 ? t1 - t0 : 0;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-
-    float* qs = sm;                 // [G][HD]
-    float* sc = sm + G * HD;        // [G][lmax]
-    for (uint32_t i = threadIdx.x; i < G * HD; i += blockDim.x) qs[i] = a.q[(size_t)kvh * G * HD + i];
-    __syncthreads();
-
-    const KVT* kb = reinterpret_cast<const KVT*>(a.k) + (size_t)kvh * a.max_seq * HD;
-    const KVT* vb = reinterpret_cast<const KVT*>(a.v) + (size_t)kvh * a.max_seq * HD;
-
-    // scores: one warp per key, lanes over head dims; 4 keys per warp in flight
-    constexpr int KU = 4;
-    for (uint32_t tb = warp; tb < nk; tb += KU * nw) {
-        float kv[KU][NV];
-#pragma unroll
-        for (int u = 0; u < KU; ++u) {
-            const uint32_t t = tb + u * nw;
-            const KVT* kr = kb + (size_t)(t0 + (t < nk ? t : 0)) * HD;
-#pragma unroll
-            for (int i = 0; i < NV; ++i) {
-                const uint32_t d = lane + 32 * i;
-                kv[u][i] = (t < nk && d < HD) ? KVConv<KVT>::to_f(kr[d]) : 0.0f;
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < KU; ++u) {
-            const uint32_t t = tb + u * nw;
-#pragma unroll
-            for (uint32_t g = 0; g < GT; ++g) {
-                if (g >= G) break;
-                float p = 0.0f;
-#pragma unroll
-                for (int i = 0; i < NV; ++i) {
-                    const uint32_t d = lane + 32 * i;
-                    if (d < HD) p = fmaf(qs[g * HD + d], kv[u][i], p);
-                }
-                p = warp_sum(p);
-                if (lane == 0 && t < nk) sc[g * a.lmax + t] = __fmul_rn(p, a.scale);
-            }
-        }
-    }
-    __syncthreads();
-    // per query head: running max and sum of exponentials (cpu_ref.hpp:55-72)
-    for (uint32_t g = warp; g < G; g += nw) {
-        float m = -INFINITY;
-        for (uint32_t t = lane; t < nk; t += 32) m = fmaxf(m, sc[g * a.lmax + t]);
-        m = warp_max(m);
-        float l = 0.0f;
-        for (uint32_t t = lane; t < nk; t += 32) {
-            const float e = expf(sc[g * a.lmax + t] - m);
-            sc[g * a.lmax + t] = e;
-            l += e;
-        }
-        l = warp_sum(l);
-        if (lane == 0) { s_m[g] = m; s_l[g] = l; }
-    }
-    __syncthreads();
-    // o = sum_t p_t v_t, threads over head dims
-    const size_t pstride = HD + 2;
-    for (uint32_t d = threadIdx.x; d < HD; d += blockDim.x) {
-        float acc[GT];
-#pragma unroll
-        for (int g = 0; g < GT; ++g) acc[g] = 0.0f;
-        uint32_t t = 0;
-        for (; t + 8 <= nk; t += 8) {  // 8 V rows in flight per thread
-            float vv[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) vv[u] = KVConv<KVT>::to_f(vb[(size_t)(t0 + t + u) * HD + d]);
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-#pragma unroll
-                for (int g = 0; g < GT; ++g)
-                    if ((uint32_t)g < G) acc[g] = fmaf(sc[g * a.lmax + t + u], vv[u], acc[g]);
-        }
-        for (; t < nk; ++t) {
-            const float vv = KVConv<KVT>::to_f(vb[(size_t)(t0 + t) * HD + d]);
-#pragma unroll
-            for (int g = 0; g < GT; ++g)
-                if ((uint32_t)g < G) acc[g] = fmaf(sc[g * a.lmax + t], vv, acc[g]);
-        }
-#pragma unroll
-        for (int g = 0; g < GT; ++g)
-            if ((uint32_t)g < G) a.part[((size_t)(kvh * G + g) * S + sidx) * pstride + 2 + d] = acc[g];
-    }
-    if (threadIdx.x < G) {
-        float* p = a.part + ((size_t)(kvh * G + threadIdx.x) * S + sidx) * pstride;
-        p[0] = s_m[threadIdx.x];
-        p[1] = s_l[threadIdx.x];
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) s_last = (atomicAdd(a.ticket + kvh, 1u) == S - 1);
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    for (uint32_t i = threadIdx.x; i < G * HD; i += blockDim.x) {
-        const uint32_t g = i / HD, d = i % HD;
-        const float* pb = a.part + (size_t)(kvh * G + g) * S * pstride;
-        float M = -INFINITY;
-        for (uint32_t s = 0; s < S; ++s)
-            if (__ldcg(pb + s * pstride + 1) > 0.0f) M = fmaxf(M, __ldcg(pb + s * pstride));
-        float l = 0.0f, o = 0.0f;
-        for (uint32_t s = 0; s < S; ++s) {
-            const float ls = __ldcg(pb + s * pstride + 1);
-            if (ls > 0.0f) {
-                const float f = expf(__ldcg(pb + s * pstride) - M);
-                l = fmaf(ls, f, l);
-                o = fmaf(__ldcg(pb + s * pstride + 2 + d), f, o);
-            }
-        }
-        a.out[(size_t)(kvh * G + g) * HD + d] = __fdiv_rn(o, l);
-    }
-    if (threadIdx.x == 0) a.ticket[kvh] = 0;
-}
-
-template <int NV, int GT, typename KVT>
-static cudaError_t launch_attn_g(const AttnArgs& a, uint32_t KVH, uint32_t S, cudaStream_t s, bool pdl) {
-    auto kern = attn_decode_kernel<NV, GT, KVT>;
-    const size_t smem = (size_t)(a.G * a.hd + a.G * a.lmax) * sizeof(float);
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) dev = 0;
-    if (!attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (e != cudaSuccess) return e;
-        attr_set[dev] = true;
-    }
-    return launch_pdl(kern, dim3(KVH, S), dim3(128), smem, s, pdl, a);
-}
-
-template <int NV, typename KVT>
-static cudaError_t launch_attn_t(const AttnArgs& a, uint32_t KVH, uint32_t S, cudaStream_t s, bool pdl) {
-    if (a.G <= 1) return launch_attn_g<NV, 1, KVT>(a, KVH, S, s, pdl);
-    if (a.G <= 2) return launch_attn_g<NV, 2, KVT>(a, KVH, S, s, pdl);
-    if (a.G <= 4) return launch_attn_g<NV, 4, KVT>(a, KVH, S, s, pdl);
-    if (a.G <= 8) return launch_attn_g<NV, 8, KVT>(a, KVH, S, s, pdl);
-    return launch_attn_g<NV, 16, KVT>(a, KVH, S, s, pdl);
-}
-
-template <typename KVT>
-static cudaError_t launch_attn(const AttnArgs& a, uint32_t KVH, uint32_t S, cudaStream_t s, bool pdl) {
-    const uint32_t nv = (a.hd + 31) / 32;
-    if (nv <= 1) return launch_attn_t<1, KVT>(a, KVH, S, s, pdl);
-    if (nv <= 2) return launch_attn_t<2, KVT>(a, KVH, S, s, pdl);
-    if (nv <= 4) return launch_attn_t<4, KVT>(a, KVH, S, s, pdl);
-    return launch_attn_t<8, KVT>(a, KVH, S, s, pdl);
-}
-
 }  // namespace bt
 
 using namespace bt;
 
 // ---------------------------------------------------------------- engine objects
 
+// Matrices in the 576-byte unit layout of bt_gemv_mma.cuh (rows padded to 16).
 struct LayerDev {
-    int8_t* qkv_q; float* qkv_s;   // [D + 2 KVD][D]   q,k rows RoPE-pair interleaved
-    int8_t* o_q;   float* o_s;     // [D][D]
-    int8_t* gu_q;  float* gu_s;    // [2F][D]          (gate, up) rows interleaved
-    int8_t* d_q;   float* d_s;     // [D][F]
+    uint8_t* qkv;   // [D + 2 KVD] x D, q and k rows as RoPE pairs (i, i + hd/2) of each head
+    uint8_t* o;     // D x D
+    uint8_t* gu;    // 2F x D, (gate, up) rows interleaved
+    uint8_t* d;     // D x F
     float* attn_norm;
     float* ffn_norm;
 };
@@ -232,15 +52,17 @@ struct bt_engine {
     cudaStream_t stream = nullptr;
     bool pdl = true;
     bool use_graph = true;
-    bool use_stream = true;   // bulk-copy streaming GEMV where the shape allows
+    uint32_t prefetch_bytes = 98304;  // L2 prefetch of the next GEMV's weights, per CTA
     uint32_t num_sms = 148;
     bool taps_on = false;
     std::vector<void*> allocs;
     std::vector<LayerDev> layers;
     float* embed = nullptr;
     float* out_norm = nullptr;
-    int8_t* head_q = nullptr;
-    float* head_s = nullptr;
+    uint8_t* head = nullptr;  // V x D units
+    // partial sums of row groups cut between two CTAs of a GEMV ([num_sms][32] + tickets)
+    float* split_part = nullptr;
+    uint32_t* split_ticket = nullptr;
     // activations
     float* x = nullptr;
     float* q = nullptr;
@@ -253,6 +75,7 @@ struct bt_engine {
     uint32_t* am_idx = nullptr;
     uint32_t* am_ticket = nullptr;
     bool loaded = false;
+    std::vector<bt_kv*> kvs;  // caches created on this engine and not yet destroyed
 };
 
 struct bt_kv {
@@ -311,6 +134,7 @@ int dev_alloc(std::vector<void*>& list, T** out, size_t count, const char* what)
     } while (0)
 
 uint32_t kvd(const bt_model_config& c) { return c.num_kv_heads * c.head_dim; }
+uint32_t pad16(uint32_t m) { return (m + 15) / 16 * 16; }
 
 int validate_config(const bt_model_config& c) {
     if (c.vocab_size == 0 || c.dim == 0 || c.hidden_dim == 0 || c.num_layers == 0 || c.num_heads == 0 ||
@@ -333,8 +157,7 @@ int validate_config(const bt_model_config& c) {
 
 // Destination of each of the 9 per-layer tensors inside the fused device layout.
 struct Slot {
-    int8_t* q;
-    float* s;
+    uint8_t* units;
     uint32_t rows, cols;
     RowMap map;
 };
@@ -344,14 +167,23 @@ Slot layer_slot(bt_engine* e, uint32_t l, int j) {
     LayerDev& L = e->layers[l];
     const uint32_t D = c.dim, F = c.hidden_dim, KV = kvd(c), hd = c.head_dim;
     switch (j) {
-        case 2: return {L.qkv_q, L.qkv_s, D, D, RowMap{1, hd, 0, 0, 0}};
-        case 3: return {L.qkv_q, L.qkv_s, KV, D, RowMap{1, hd, 0, 0, D}};
-        case 4: return {L.qkv_q, L.qkv_s, KV, D, RowMap{0, 0, 0, 0, D + KV}};
-        case 5: return {L.o_q, L.o_s, D, D, RowMap{0, 0, 0, 0, 0}};
-        case 6: return {L.gu_q, L.gu_s, F, D, RowMap{2, 0, 0, 0, 0}};
-        case 7: return {L.gu_q, L.gu_s, F, D, RowMap{2, 0, 1, 0, 0}};
-        default: return {L.d_q, L.d_s, D, F, RowMap{0, 0, 0, 0, 0}};
+        case 2: return {L.qkv, D, D, RowMap{1, hd, 0, 0, 0}};
+        case 3: return {L.qkv, KV, D, RowMap{1, hd, 0, 0, D}};
+        case 4: return {L.qkv, KV, D, RowMap{0, 0, 0, 0, D + KV}};
+        case 5: return {L.o, D, D, RowMap{0, 0, 0, 0, 0}};
+        case 6: return {L.gu, F, D, RowMap{2, 0, 0, 0, 0}};
+        case 7: return {L.gu, F, D, RowMap{2, 0, 1, 0, 0}};
+        default: return {L.d, D, F, RowMap{0, 0, 0, 0, 0}};
     }
+}
+
+// Unit-layout matrix of M x K rows (padding rows zero).
+int alloc_units(bt_engine* e, uint8_t** out, uint32_t M, uint32_t K, const char* what) {
+    const uint64_t bytes = unit_bytes(M, K);
+    int rc = dev_alloc(e->allocs, out, bytes, what);
+    if (rc != BT_OK) return rc;
+    BT_CUDA_CHECK(cudaMemsetAsync(*out, 0, bytes, e->stream));
+    return BT_OK;
 }
 
 int alloc_weights(bt_engine* e) {
@@ -360,20 +192,15 @@ int alloc_weights(bt_engine* e) {
     auto& A = e->allocs;
     BT_TRY_ALLOC(A, &e->embed, V * D, "embed");
     BT_TRY_ALLOC(A, &e->out_norm, D, "out_norm");
-    BT_TRY_ALLOC(A, &e->head_q, V * D, "head qs");
-    BT_TRY_ALLOC(A, &e->head_s, V * D / 32, "head scales");
+    int rc = alloc_units(e, &e->head, (uint32_t)V, (uint32_t)D, "head");
+    if (rc != BT_OK) return rc;
     e->layers.resize(c.num_layers);
     for (uint32_t l = 0; l < c.num_layers; ++l) {
         LayerDev& L = e->layers[l];
-        const size_t Mqkv = D + 2 * KV;
-        BT_TRY_ALLOC(A, &L.qkv_q, Mqkv * D, "wqkv");
-        BT_TRY_ALLOC(A, &L.qkv_s, Mqkv * D / 32, "wqkv scales");
-        BT_TRY_ALLOC(A, &L.o_q, D * D, "wo");
-        BT_TRY_ALLOC(A, &L.o_s, D * D / 32, "wo scales");
-        BT_TRY_ALLOC(A, &L.gu_q, 2 * F * D, "wgu");
-        BT_TRY_ALLOC(A, &L.gu_s, 2 * F * D / 32, "wgu scales");
-        BT_TRY_ALLOC(A, &L.d_q, D * F, "wd");
-        BT_TRY_ALLOC(A, &L.d_s, D * F / 32, "wd scales");
+        if ((rc = alloc_units(e, &L.qkv, (uint32_t)(D + 2 * KV), (uint32_t)D, "wqkv"))) return rc;
+        if ((rc = alloc_units(e, &L.o, (uint32_t)D, (uint32_t)D, "wo"))) return rc;
+        if ((rc = alloc_units(e, &L.gu, (uint32_t)(2 * F), (uint32_t)D, "wgu"))) return rc;
+        if ((rc = alloc_units(e, &L.d, (uint32_t)D, (uint32_t)F, "wd"))) return rc;
         BT_TRY_ALLOC(A, &L.attn_norm, D, "attn_norm");
         BT_TRY_ALLOC(A, &L.ffn_norm, D, "ffn_norm");
     }
@@ -388,6 +215,9 @@ int alloc_weights(bt_engine* e) {
     BT_TRY_ALLOC(A, &e->am_idx, nblk, "argmax idx");
     BT_TRY_ALLOC(A, &e->am_ticket, 4, "argmax ticket");
     BT_CUDA_CHECK(cudaMemsetAsync(e->am_ticket, 0, 16, e->stream));
+    BT_TRY_ALLOC(A, &e->split_part, (size_t)e->num_sms * 32, "split partials");
+    BT_TRY_ALLOC(A, &e->split_ticket, (size_t)e->num_sms, "split tickets");
+    BT_CUDA_CHECK(cudaMemsetAsync(e->split_ticket, 0, sizeof(uint32_t) * e->num_sms, e->stream));
     return BT_OK;
 }
 
@@ -396,6 +226,16 @@ void drop_graphs_of(bt_kv* kv) {
         cudaGraphExecDestroy(kv->graph);
         kv->graph = nullptr;
     }
+}
+
+// Frees the device side of a cache (graph, buffers, pinned staging); the handle stays.
+void release_kv_device(bt_kv* kv) {
+    drop_graphs_of(kv);
+    for (void* p : kv->allocs) cudaFree(p);
+    kv->allocs.clear();
+    if (kv->h_st) cudaFreeHost(kv->h_st);
+    kv->h_st = nullptr;
+    kv->k = kv->v = nullptr;
 }
 
 // Events recorded after every launch of a step (per-kernel profiling; no PDL).
@@ -415,8 +255,14 @@ int enqueue_step(bt_engine* e, bt_kv* kv, cudaStream_t s, Marks* marks = nullptr
     const uint32_t D = c.dim, F = c.hidden_dim, KV = kvd(c), hd = c.head_dim;
     const uint32_t G = c.num_heads / c.num_kv_heads;
     const bool pdl = e->pdl && !marks;
-    const bool stream = e->use_stream;
     const uint32_t nsm = e->num_sms;
+    const SplitScratch sp{e->split_part, e->split_ticket};
+    const uint32_t QKV = D + 2 * KV;
+    // the GEMV that follows each one, for the producer's L2 prefetch
+    auto next = [&](const uint8_t* u, uint32_t M, uint32_t K) {
+        return e->prefetch_bytes ? NextW{u, pad16(M), K, mma_grid(pad16(M), nsm), e->prefetch_bytes}
+                                 : NextW{nullptr, 0, 0, 0, 0};
+    };
     uint32_t* errp = &kv->st->error;
     const size_t kv_layer = (size_t)c.num_kv_heads * kv->max_seq * hd;
     const size_t esz = kv->dtype == BT_KV_FP16 ? 2 : 4;
@@ -427,60 +273,54 @@ int enqueue_step(bt_engine* e, bt_kv* kv, cudaStream_t s, Marks* marks = nullptr
         char* vl = static_cast<char*>(kv->v) + l * kv_layer * esz;
         // qkv
         {
-            GemvW g{L.qkv_q, L.qkv_s, D + 2 * KV, D};
-            ProNorm pro{e->x, L.attn_norm, c.rms_norm_eps, l == 0 ? e->embed : nullptr, kv->st, e->x};
-            SProNorm spro{e->x, L.attn_norm, c.rms_norm_eps, l == 0 ? e->embed : nullptr, kv->st, e->x};
+            const UnitW w{L.qkv, QKV, pad16(QKV), D};
+            const NextW nx = next(L.o, D, D);
+            MProNorm pro{e->x, L.attn_norm, c.rms_norm_eps, l == 0 ? e->embed : nullptr, kv->st, e->x};
             cudaError_t err;
             if (kv->dtype == BT_KV_FP16) {
                 EpiQKV<__half> epi{e->q, reinterpret_cast<__half*>(kl), reinterpret_cast<__half*>(vl), kv->rope, kv->st,
                                    D, KV, hd, kv->max_seq};
-                err = launch_gemv_best(g, spro, SEpiQKV<__half>{epi}, pro, epi, true, errp, nsm, s, pdl, stream);
+                err = launch_gemv_mma(w, pro, SEpiQKV<__half>{epi}, sp, errp, nsm, s, pdl, nx);
             } else {
                 EpiQKV<float> epi{e->q, reinterpret_cast<float*>(kl), reinterpret_cast<float*>(vl), kv->rope, kv->st,
                                   D, KV, hd, kv->max_seq};
-                err = launch_gemv_best(g, spro, SEpiQKV<float>{epi}, pro, epi, true, errp, nsm, s, pdl, stream);
+                err = launch_gemv_mma(w, pro, SEpiQKV<float>{epi}, sp, errp, nsm, s, pdl, nx);
             }
             BT_CUDA_CHECK(err);
             BT_MARK();
         }
         // attention
         {
-            AttnArgs a{e->q, kl, vl, e->attn, kv->att_part, kv->att_ticket + l * c.num_kv_heads, kv->st,
-                       hd, G, kv->max_seq, kv->lmax, scale};
+            AttnArgs a{e->q, kl, vl, e->attn, kv->att_part, kv->att_ticket + l * c.num_kv_heads, kv->st, errp,
+                       hd, G, kv->max_seq, kv->lmax, 0, scale, (hd * esz) % 16 == 0 ? 1 : 0};
             cudaError_t err = kv->dtype == BT_KV_FP16 ? launch_attn<__half>(a, c.num_kv_heads, kv->splits, s, pdl)
                                                        : launch_attn<float>(a, c.num_kv_heads, kv->splits, s, pdl);
             BT_CUDA_CHECK(err);
             BT_MARK();
         }
         // o-proj + residual
-        {
-            EpiResidual epi{e->x, nullptr};
-            BT_CUDA_CHECK(launch_gemv_best(GemvW{L.o_q, L.o_s, D, D}, SProCopy{e->attn}, SEpiResidual{e->x, nullptr},
-                                           ProCopy{e->attn}, epi, false, errp, nsm, s, pdl, stream));
-            BT_MARK();
-        }
+        BT_CUDA_CHECK(launch_gemv_mma(UnitW{L.o, D, pad16(D), D}, MProCopy{e->attn}, SEpiResidual{e->x, nullptr}, sp,
+                                      errp, nsm, s, pdl, next(L.gu, 2 * F, D)));
+        BT_MARK();
         // gate/up + SwiGLU
-        {
-            ProNorm pro{e->x, L.ffn_norm, c.rms_norm_eps, nullptr, nullptr, nullptr};
-            SProNorm spro{e->x, L.ffn_norm, c.rms_norm_eps, nullptr, nullptr, nullptr};
-            BT_CUDA_CHECK(launch_gemv_best(GemvW{L.gu_q, L.gu_s, 2 * F, D}, spro, SEpiSwiGLU{e->act}, pro,
-                                           EpiSwiGLU{e->act}, true, errp, nsm, s, pdl, stream));
-            BT_MARK();
-        }
+        BT_CUDA_CHECK(launch_gemv_mma(UnitW{L.gu, 2 * F, pad16(2 * F), D},
+                                      MProNorm{e->x, L.ffn_norm, c.rms_norm_eps, nullptr, nullptr, nullptr},
+                                      SEpiSwiGLU{e->act}, sp, errp, nsm, s, pdl, next(L.d, D, F)));
+        BT_MARK();
         // down + residual (+ tap)
         {
             float* tap = e->taps_on ? e->taps + (size_t)l * D : nullptr;
-            BT_CUDA_CHECK(launch_gemv_best(GemvW{L.d_q, L.d_s, D, F}, SProCopy{e->act}, SEpiResidual{e->x, tap},
-                                           ProCopy{e->act}, EpiResidual{e->x, tap}, false, errp, nsm, s, pdl, stream));
+            const NextW nx = l + 1 < c.num_layers ? next(e->layers[l + 1].qkv, QKV, D) : next(e->head, c.vocab_size, D);
+            BT_CUDA_CHECK(launch_gemv_mma(UnitW{L.d, D, pad16(D), F}, MProCopy{e->act}, SEpiResidual{e->x, tap}, sp,
+                                          errp, nsm, s, pdl, nx));
             BT_MARK();
         }
     }
     {
-        ProNorm pro{e->x, e->out_norm, c.rms_norm_eps, nullptr, nullptr, nullptr};
-        SProNorm spro{e->x, e->out_norm, c.rms_norm_eps, nullptr, nullptr, nullptr};
         EpiLogits epi{e->logits, e->am_val, e->am_idx, e->am_ticket, kv->st, kv->tok_hist, kv->max_seq};
-        BT_CUDA_CHECK(launch_gemv_best(GemvW{e->head_q, e->head_s, c.vocab_size, D}, spro, SEpiLogits{epi}, pro, epi,
-                                       false, errp, nsm, s, pdl, stream));
+        BT_CUDA_CHECK(launch_gemv_mma(UnitW{e->head, c.vocab_size, pad16(c.vocab_size), D},
+                                      MProNorm{e->x, e->out_norm, c.rms_norm_eps, nullptr, nullptr, nullptr},
+                                      SEpiLogits{epi}, sp, errp, nsm, s, pdl, next(e->layers[0].qkv, QKV, D)));
         BT_MARK();
     }
     return BT_OK;
@@ -562,7 +402,10 @@ int bt_engine_create(int device, const bt_model_config* cfg, const bt_engine_opt
     if (opt && opt->rope_theta > 0.0f) e->theta = opt->rope_theta;
     if (const char* v = std::getenv("BT_NO_PDL")) e->pdl = (v[0] == '0');
     if (const char* v = std::getenv("BT_NO_GRAPH")) e->use_graph = (v[0] == '0');
-    if (const char* v = std::getenv("BT_NO_STREAM")) e->use_stream = (v[0] == '0');
+    if (const char* v = std::getenv("BT_GEMV_PREFETCH_KB")) {
+        const long kb = std::atol(v);
+        if (kb >= 0 && kb <= 1024) e->prefetch_bytes = (uint32_t)kb * 1024;
+    }
     int nsm = 0;
     BT_CUDA_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device));
     e->num_sms = nsm > 0 ? (uint32_t)nsm : 148;
@@ -582,6 +425,13 @@ int bt_engine_destroy(bt_engine* e) {
     if (!e) return BT_OK;
     DeviceGuard guard(e->device);
     if (e->stream) cudaStreamSynchronize(e->stream);
+    // caches still alive are detached: their device memory goes with the engine,
+    // and a later bt_kv_destroy only frees the handle
+    for (bt_kv* kv : e->kvs) {
+        release_kv_device(kv);
+        kv->e = nullptr;
+    }
+    e->kvs.clear();
     for (void* p : e->allocs) cudaFree(p);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
@@ -623,17 +473,17 @@ int bt_engine_load(bt_engine* e, const bt_tensor_view* t, uint32_t n, int on_dev
     for (size_t b : {qbytes(F, D), qbytes(D, F)}) max_q = b > max_q ? b : max_q;
     void* stage = nullptr;
     if (!on_device) BT_CUDA_CHECK(cudaMalloc(&stage, max_q));
-    auto load_q = [&](const bt_tensor_view& tv, int8_t* q, float* sc, uint32_t rows, uint32_t cols, RowMap m) -> int {
+    auto load_q = [&](const bt_tensor_view& tv, uint8_t* units, uint32_t rows, uint32_t cols, RowMap m) -> int {
         const void* src = tv.data;
         if (!on_device) {
             BT_CUDA_CHECK(cudaMemcpyAsync(stage, tv.data, tv.bytes, cudaMemcpyHostToDevice, s));
             src = stage;
         }
-        BT_CUDA_CHECK(launch_repack_q8_0(src, q, sc, rows, cols, m, s));
+        BT_CUDA_CHECK(launch_pack_units(src, units, rows, cols, m, s));
         if (!on_device) BT_CUDA_CHECK(cudaStreamSynchronize(s));  // stage is reused
         return BT_OK;
     };
-    rc = load_q(t[2], e->head_q, e->head_s, c.vocab_size, c.dim, RowMap{0, 0, 0, 0, 0});
+    rc = load_q(t[2], e->head, c.vocab_size, c.dim, RowMap{0, 0, 0, 0, 0});
     for (uint32_t l = 0; rc == BT_OK && l < c.num_layers; ++l) {
         LayerDev& L = e->layers[l];
         const bt_tensor_view* tl = t + 3 + 9 * l;
@@ -642,7 +492,7 @@ int bt_engine_load(bt_engine* e, const bt_tensor_view* t, uint32_t n, int on_dev
         if (ce != cudaSuccess) { rc = fail(BT_ERR_CUDA, cudaGetErrorString(ce)); break; }
         for (int j = 2; j < 9 && rc == BT_OK; ++j) {
             Slot sl = layer_slot(e, l, j);
-            rc = load_q(tl[j], sl.q, sl.s, sl.rows, sl.cols, sl.map);
+            rc = load_q(tl[j], sl.units, sl.rows, sl.cols, sl.map);
         }
     }
     cudaError_t ce = cudaStreamSynchronize(s);
@@ -671,7 +521,7 @@ int bt_engine_generate(bt_engine* e, uint64_t seed, float sigma) {
         return fail(BT_ERR_OUT_OF_MEMORY, "bt_engine_generate: staging allocation failed");
     }
     int rc = BT_OK;
-    auto gen_q = [&](uint32_t stream_id, int8_t* q, float* sc, size_t rows, size_t cols, RowMap m) -> int {
+    auto gen_q = [&](uint32_t stream_id, uint8_t* units, size_t rows, size_t cols, RowMap m) -> int {
         const size_t rows_per = slab / cols;
         for (size_t r0 = 0; r0 < rows; r0 += rows_per) {
             const size_t nr = (rows - r0) < rows_per ? (rows - r0) : rows_per;
@@ -679,14 +529,14 @@ int bt_engine_generate(bt_engine* e, uint64_t seed, float sigma) {
             BT_CUDA_CHECK(launch_quantize_q8_0(tmp, blk, nr * cols / 32, s));
             RowMap mm = m;
             mm.src_off = (uint32_t)r0;
-            BT_CUDA_CHECK(launch_repack_q8_0(blk, q, sc, (uint32_t)nr, (uint32_t)cols, mm, s));
+            BT_CUDA_CHECK(launch_pack_units(blk, units, (uint32_t)nr, (uint32_t)cols, mm, s));
         }
         return BT_OK;
     };
     ce = launch_gen_normal(seed, 0, 0, V * D, k, e->embed, s);
     if (ce == cudaSuccess) ce = launch_fill(e->out_norm, D, 1.0f, s);
     if (ce != cudaSuccess) rc = fail(BT_ERR_CUDA, cudaGetErrorString(ce));
-    if (rc == BT_OK) rc = gen_q(2, e->head_q, e->head_s, V, D, RowMap{0, 0, 0, 0, 0});
+    if (rc == BT_OK) rc = gen_q(2, e->head, V, D, RowMap{0, 0, 0, 0, 0});
     for (uint32_t l = 0; rc == BT_OK && l < c.num_layers; ++l) {
         LayerDev& L = e->layers[l];
         ce = launch_fill(L.attn_norm, D, 1.0f, s);
@@ -694,7 +544,7 @@ int bt_engine_generate(bt_engine* e, uint64_t seed, float sigma) {
         if (ce != cudaSuccess) { rc = fail(BT_ERR_CUDA, cudaGetErrorString(ce)); break; }
         for (int j = 2; j < 9 && rc == BT_OK; ++j) {
             Slot sl = layer_slot(e, l, j);
-            rc = gen_q(16 + 16 * l + j, sl.q, sl.s, sl.rows, sl.cols, sl.map);
+            rc = gen_q(16 + 16 * l + j, sl.units, sl.rows, sl.cols, sl.map);
         }
     }
     (void)KV; (void)F;
@@ -737,14 +587,10 @@ int bt_kv_create(bt_engine* e, uint32_t max_seq, int dtype, bt_kv** out) {
     if ((rc = dev_alloc(kv->allocs, &kv->rope, (size_t)max_seq * half, "rope table"))) return cleanup(rc);
     if ((rc = dev_alloc(kv->allocs, &kv->st, 1, "state"))) return cleanup(rc);
     if ((rc = dev_alloc(kv->allocs, &kv->tok_hist, (size_t)max_seq + 1, "token history"))) return cleanup(rc);
-    // attention split count: >= 2 CTAs per SM over all KV heads, <= 256 keys per split
-    uint32_t S = (296 + c.num_kv_heads - 1) / c.num_kv_heads;
-    const uint32_t s2 = (max_seq + 255) / 256;
-    if (s2 > S) S = s2;
-    if (S > max_seq) S = max_seq;
-    if (S < 1) S = 1;
-    kv->splits = S;
-    kv->lmax = (max_seq + S - 1) / S;
+    // attention splits: >= 2 CTAs per SM over the KV heads, K+V tiles <= 32 KB per CTA
+    attn_plan(c.num_kv_heads, c.head_dim, c.num_heads / c.num_kv_heads, max_seq, esz, e->num_sms, kv->splits,
+              kv->lmax);
+    const uint32_t S = kv->splits;
     if ((rc = dev_alloc(kv->allocs, &kv->att_part, (size_t)c.num_heads * S * (c.head_dim + 2), "attention partials")))
         return cleanup(rc);
     if ((rc = dev_alloc(kv->allocs, &kv->att_ticket, (size_t)c.num_layers * c.num_kv_heads, "attention tickets")))
@@ -768,23 +614,31 @@ int bt_kv_create(bt_engine* e, uint32_t max_seq, int dtype, bt_kv** out) {
     if (ce == cudaSuccess) ce = cudaMallocHost(&kv->h_st, sizeof(DevState));
     if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->stream);
     if (ce != cudaSuccess) return cleanup(fail(BT_ERR_CUDA, cudaGetErrorString(ce)));
+    e->kvs.push_back(kv.get());
     *out = kv.release();
     return BT_OK;
 }
 
 int bt_kv_destroy(bt_kv* kv) {
     if (!kv) return BT_OK;
-    DeviceGuard guard(kv->e->device);
-    cudaStreamSynchronize(kv->e->stream);
-    drop_graphs_of(kv);
-    for (void* p : kv->allocs) cudaFree(p);
-    if (kv->h_st) cudaFreeHost(kv->h_st);
+    if (kv->e) {  // still attached: free its device memory and unregister it
+        bt_engine* e = kv->e;
+        DeviceGuard guard(e->device);
+        cudaStreamSynchronize(e->stream);
+        release_kv_device(kv);
+        for (size_t i = 0; i < e->kvs.size(); ++i)
+            if (e->kvs[i] == kv) {
+                e->kvs.erase(e->kvs.begin() + (long)i);
+                break;
+            }
+    }
     delete kv;
     return BT_OK;
 }
 
 int bt_kv_read_layer(bt_kv* kv, uint32_t layer, float* k, float* v) {
     if (!kv || !k || !v) return fail(BT_ERR_INVALID_ARGUMENT, "bt_kv_read_layer: null argument");
+    if (!kv->e) return fail(BT_ERR_INVALID_ARGUMENT, "KV cache outlived its engine");
     bt_engine* e = kv->e;
     const auto& c = e->cfg;
     if (layer >= c.num_layers) return fail(BT_ERR_OUT_OF_RANGE, "KVCache layer out of bounds");
@@ -901,6 +755,7 @@ int bt_engine_read_taps(bt_engine* e, float* taps) {
 
 int bt_kv_step_info(bt_kv* kv, uint32_t context, uint64_t* launches, uint64_t* bytes) {
     if (!kv) return fail(BT_ERR_INVALID_ARGUMENT, "null KV cache");
+    if (!kv->e) return fail(BT_ERR_INVALID_ARGUMENT, "KV cache outlived its engine");
     const auto& c = kv->e->cfg;
     const uint64_t D = c.dim, F = c.hidden_dim, KV = kvd(c), V = c.vocab_size, L = c.num_layers;
     const uint64_t params = L * (D * D * 2 + KV * D * 2 + F * D * 3) + V * D;
@@ -916,6 +771,7 @@ int bt_kv_step_info(bt_kv* kv, uint32_t context, uint64_t* launches, uint64_t* b
 
 int bt_kv_state(bt_kv* kv, uint32_t* pos, uint32_t* token, uint32_t* last_argmax) {
     if (!kv) return fail(BT_ERR_INVALID_ARGUMENT, "null KV cache");
+    if (!kv->e) return fail(BT_ERR_INVALID_ARGUMENT, "KV cache outlived its engine");
     DeviceGuard guard(kv->e->device);
     DevState h{};
     BT_CUDA_CHECK(cudaStreamSynchronize(kv->e->stream));

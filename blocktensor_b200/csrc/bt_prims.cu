@@ -6,10 +6,49 @@
 // kernel-level parity tests.
 #include "bt_common.cuh"
 #include "bt_gemv.cuh"
-#include "bt_gemv_stream.cuh"
+#include "bt_gemv_mma.cuh"
 #include "bt_internal.h"
 
+#include <mutex>
+
 namespace bt {
+
+// Per-device workspace of the standalone tensor-core GEMV: partial sums of
+// row groups cut between two CTAs ([num_sms][32] floats), their tickets
+// ([num_sms], zero between launches) and the bounded-wait error flag.
+struct GemvWorkspace {
+    float* part = nullptr;
+    uint32_t* ticket = nullptr;  // num_sms tickets followed by the error flag
+    uint32_t nsm = 0;
+};
+
+static std::mutex g_ws_mutex;
+static GemvWorkspace g_ws[64];
+
+static int gemv_workspace(int dev, GemvWorkspace** out) {
+    if (dev < 0 || dev >= 64) return fail(BT_ERR_INVALID_ARGUMENT, "gemv workspace: device index out of range");
+    std::lock_guard<std::mutex> lock(g_ws_mutex);
+    GemvWorkspace& w = g_ws[dev];
+    if (!w.part) {
+        int nsm = 0;
+        BT_CUDA_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+        float* part = nullptr;
+        uint32_t* ticket = nullptr;
+        BT_CUDA_CHECK(cudaMalloc(&part, sizeof(float) * 32 * nsm));
+        cudaError_t e = cudaMalloc(&ticket, sizeof(uint32_t) * (nsm + 1));
+        if (e == cudaSuccess) e = cudaMemset(ticket, 0, sizeof(uint32_t) * (nsm + 1));
+        if (e != cudaSuccess) {
+            cudaFree(part);
+            if (ticket) cudaFree(ticket);
+            return fail(BT_ERR_CUDA, std::string("gemv workspace: ") + cudaGetErrorString(e));
+        }
+        w.part = part;
+        w.ticket = ticket;
+        w.nsm = (uint32_t)nsm;
+    }
+    *out = &w;
+    return BT_OK;
+}
 
 // cpu_ref::rmsnorm (cpu_ref.hpp:11-28): one CTA per row.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ in, const float* __restrict__ w,
@@ -320,6 +359,24 @@ int bt_cuda_matvec_q8_0(const void* W_blocks, const float* X, float* Y, uint32_t
     return BT_OK;
 }
 
+int bt_cuda_gemv_q8_units(const void* units, const float* x, float* y, uint32_t M, uint32_t K, void* stream) {
+    BT_CHECK_ARG(K % 32 == 0 && K > 0, "gemv_q8_units: K must be a positive multiple of 32");
+    BT_CHECK_ARG(K <= 48 * 1024, "gemv_q8_units: K above 49152 not supported");
+    BT_CHECK_ARG(units && x && y, "gemv_q8_units: null buffer");
+    BT_CHECK_ARG(((uintptr_t)units & 15) == 0 && ((uintptr_t)x & 15) == 0,
+                 "gemv_q8_units: units and x must be 16-byte aligned");
+    if (M == 0) return BT_OK;
+    int dev = 0;
+    BT_CUDA_CHECK(cudaGetDevice(&dev));
+    GemvWorkspace* ws = nullptr;
+    int rc = gemv_workspace(dev, &ws);
+    if (rc != BT_OK) return rc;
+    const UnitW w{static_cast<const uint8_t*>(units), M, (M + 15) / 16 * 16, K};
+    BT_CUDA_CHECK(launch_gemv_mma(w, MProCopy{x}, SEpiStore{y}, SplitScratch{ws->part, ws->ticket},
+                                  ws->ticket + ws->nsm, ws->nsm, as_stream(stream), false));
+    return BT_OK;
+}
+
 int bt_cuda_gemv_q8(const int8_t* qs, const float* scales, const float* X, float* Y, uint32_t M, uint32_t K,
                     uint32_t B, void* stream) {
     BT_CHECK_ARG(K % 32 == 0, "gemv_q8: K must be a multiple of 32");
@@ -331,16 +388,7 @@ int bt_cuda_gemv_q8(const int8_t* qs, const float* scales, const float* X, float
     if (M == 0) return BT_OK;
     cudaStream_t s = as_stream(stream);
     cudaError_t e;
-    if (B == 1) {
-        static int nsm_cache[64] = {};
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (dev < 0 || dev >= 64) dev = 0;
-        if (!nsm_cache[dev]) cudaDeviceGetAttribute(&nsm_cache[dev], cudaDevAttrMultiProcessorCount, dev);
-        const GemvW g{qs, scales, M, K};
-        e = launch_gemv_best(g, SProCopy{X}, SEpiStore{Y}, ProCopy{X}, EpiStore{Y}, false, nullptr,
-                             (uint32_t)nsm_cache[dev], s, false, true);
-    }
+    if (B == 1) e = launch_gemv(GemvW{qs, scales, M, K}, ProCopy{X}, EpiStore{Y}, s, false);
     else if (B == 2) e = launch_gemv_batch<2>(qs, scales, X, Y, M, K, B, s);
     else if (B <= 4) e = launch_gemv_batch<4>(qs, scales, X, Y, M, K, B, s);
     else if (B <= 8) e = launch_gemv_batch<8>(qs, scales, X, Y, M, K, B, s);

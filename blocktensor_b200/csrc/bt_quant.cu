@@ -93,6 +93,31 @@ __global__ void repack_q8_0_kernel(const uint8_t* __restrict__ blocks, int8_t* _
     out[1] = make_int4((int)w[5], (int)w[6], (int)w[7], (int)w[8]);
 }
 
+// One thread per (row, 32-block) of a 36-byte-block matrix -> the 576-byte unit
+// layout of the tensor-core GEMV: destination row dr lands in group dr/16, row
+// rl = dr%16 of the unit; its 32 int8 go to the mma A-fragment slots (lane
+// (rl%8)*4 + tig, register 2*kh + rl/8 holds columns 16*kh + 4*tig .. +3) and
+// its scale to float 2*(rl%8) + rl/8 after the 512 weight bytes (rows r and
+// r+8 adjacent).  Padding rows stay zero.
+__global__ void pack_units_kernel(const uint8_t* __restrict__ blocks, uint8_t* __restrict__ units, uint32_t M,
+                                  uint32_t K, RowMap map) {
+    const uint64_t nb = (uint64_t)M * (K / 32);
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nb) return;
+    const uint32_t bpr = K / 32;
+    const uint32_t r = (uint32_t)(i / bpr), b = (uint32_t)(i % bpr);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(blocks + i * 36);
+    const uint32_t dr = map_row(r, map);
+    const uint32_t rl = dr % 16, grp = rl % 8, upper = rl / 8;
+    uint8_t* unit = units + ((uint64_t)(dr / 16) * bpr + b) * 576;
+    reinterpret_cast<uint32_t*>(unit + 512)[grp * 2 + upper] = w[0];  // scales as (r, r + 8) pairs
+#pragma unroll
+    for (uint32_t kh = 0; kh < 2; ++kh)
+#pragma unroll
+        for (uint32_t tig = 0; tig < 4; ++tig)
+            *reinterpret_cast<uint32_t*>(unit + (grp * 4 + tig) * 16 + (kh * 2 + upper) * 4) = w[1 + kh * 4 + tig];
+}
+
 __device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
     z += 0x9E3779B97F4A7C15ull;
     z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
@@ -161,6 +186,15 @@ cudaError_t launch_repack_q8_0(const void* blocks, int8_t* qs, float* scales, ui
     return cudaGetLastError();
 }
 
+cudaError_t launch_pack_units(const void* blocks, uint8_t* units, uint32_t M, uint32_t K, RowMap map,
+                              cudaStream_t s) {
+    const uint64_t nb = (uint64_t)M * (K / 32);
+    if (nb == 0) return cudaSuccess;
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    pack_units_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, s>>>((const uint8_t*)blocks, units, M, K, map);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_gen_normal(uint64_t seed, uint64_t stream_id, uint64_t offset, uint64_t n, float k,
                               float* out, cudaStream_t s) {
     if (n == 0) return cudaSuccess;
@@ -199,6 +233,17 @@ int bt_cuda_dequantize_q8_0(const void* src_blocks, float* dst, uint64_t n, void
     BT_CHECK_ARG(n == 0 || (src_blocks && dst), "dequantize_q8_0: null buffer");
     BT_CHECK_ARG(((uintptr_t)src_blocks & 3) == 0, "dequantize_q8_0: src must be 4-byte aligned");
     BT_CUDA_CHECK(launch_dequantize_q8_0(src_blocks, dst, n, as_stream(stream)));
+    return BT_OK;
+}
+
+int bt_cuda_pack_q8_units(const void* W_blocks, void* units, uint32_t M, uint32_t K, void* stream) {
+    BT_CHECK_ARG(K % 32 == 0, "pack_q8_units: K must be a multiple of 32");
+    BT_CHECK_ARG(W_blocks && units, "pack_q8_units: null buffer");
+    BT_CHECK_ARG(((uintptr_t)W_blocks & 3) == 0 && ((uintptr_t)units & 15) == 0,
+                 "pack_q8_units: misaligned buffer (blocks 4 B, units 16 B)");
+    BT_CUDA_CHECK(cudaMemsetAsync(units, 0, unit_bytes(M, K), as_stream(stream)));
+    BT_CUDA_CHECK(launch_pack_units(W_blocks, static_cast<uint8_t*>(units), M, K, RowMap{0, 0, 0, 0, 0},
+                                    as_stream(stream)));
     return BT_OK;
 }
 

@@ -80,6 +80,8 @@ SIGNATURES = {
     "bt_cuda_matvec_q8_0": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp]),
     "bt_cuda_repack_q8_0": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp]),
     "bt_cuda_gemv_q8": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp]),
+    "bt_cuda_pack_q8_units": (_i32, [_vp, _vp, _u32, _u32, _vp]),
+    "bt_cuda_gemv_q8_units": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp]),
     "bt_cuda_rmsnorm": (_i32, [_vp, _vp, _vp, _u32, _u32, _f32, _vp]),
     "bt_cuda_rope": (_i32, [_vp, _vp, _u32, _u32, _u32, _u32, _f32, _vp]),
     "bt_cuda_softmax": (_i32, [_vp, _vp, _u32, _u32, _vp]),

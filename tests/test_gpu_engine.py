@@ -131,6 +131,20 @@ def test_engine_errors(cuda, tiny):
         cuda.TransformerEngine(bad)
 
 
+def test_kv_outliving_engine(cuda):
+    """Destroying the engine first detaches its caches; using one then fails cleanly."""
+    d = dict(vocab=64, dim=64, hidden=128, layers=1, heads=2, kv_heads=2, head_dim=32, max_seq=8)
+    cfg = cuda.model_config(*d.values())
+    eng = cuda.TransformerEngine(cfg)
+    eng.generate(seed=1)
+    kv = cuda.KVCache(eng, 8)
+    eng.forward_single_token(3, 0, kv)
+    eng.close()
+    with pytest.raises(ValueError):
+        kv.read_layer(0)
+    kv.close()
+
+
 def test_btmodel_file_drives_engine(cuda, oracle, tmp_path):
     """A .btmodel file (reference format) loaded into the CUDA engine matches the reference engine."""
     from blocktensor_b200 import btmodel

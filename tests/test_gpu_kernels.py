@@ -139,3 +139,36 @@ def test_launch_counter_moves(cuda, torch_mod):
     cuda.silu(torch_mod.ones(64, device="cuda"))
     torch_mod.cuda.synchronize()
     assert cuda.launch_count() == before + 1
+
+
+@pytest.mark.parametrize("M,K", [(4096, 4096), (22016, 4096), (4096, 11008), (32000, 4096), (33, 288),
+                                 (864, 288), (100, 64), (1000, 2816), (5, 32)])
+def test_gemv_units_vs_oracle(cuda, oracle, torch_mod, M, K):
+    """Tensor-core unit-layout GEMV (the engine's) against the reference matvec arithmetic."""
+    rng = np.random.default_rng(M * 7 + K)
+    b = oracle.quantize_q8_0((rng.standard_normal(M * K) * 0.02).astype(np.float32))
+    x = rng.standard_normal(K).astype(np.float32)
+    want = oracle.matvec_q8_0(b, x, M, K, nthreads=8)
+    units = cuda.pack_q8_units(dev(torch_mod, b.view(np.uint8)), M, K)
+    got = cuda.gemv_q8_units(units, dev(torch_mod, x), M, K).cpu().numpy()
+    # |sum_b s_b sum_i q_i x_i| bound: the error budget is relative to sum |s q x|
+    mag = np.abs(b["scale"].reshape(M, K // 32, 1) * b["qs"].reshape(M, K // 32, 32).astype(np.float64)
+                 * np.abs(x.reshape(1, K // 32, 32))).sum(axis=(1, 2))
+    err = np.abs(got.astype(np.float64) - want)
+    assert (err <= 1e-5 * mag + 1e-30).all(), f"worst relative error {np.max(err / (mag + 1e-30))}"
+
+
+def test_gemv_units_deterministic_and_repeatable(cuda, oracle, torch_mod):
+    M, K = 4096, 4096
+    rng = np.random.default_rng(5)
+    b = oracle.quantize_q8_0((rng.standard_normal(M * K) * 0.02).astype(np.float32))
+    units = cuda.pack_q8_units(dev(torch_mod, b.view(np.uint8)), M, K)
+    x = dev(torch_mod, rng.standard_normal(K).astype(np.float32))
+    a = cuda.gemv_q8_units(units, x, M, K).cpu().numpy()
+    for _ in range(3):
+        assert np.array_equal(cuda.gemv_q8_units(units, x, M, K).cpu().numpy(), a)
+    # zero vector -> exact zeros; scaling x by 2 doubles y exactly (power-of-two invariance)
+    z = cuda.gemv_q8_units(units, torch_mod.zeros(K, device="cuda"), M, K).cpu().numpy()
+    assert (z == 0).all()
+    a2 = cuda.gemv_q8_units(units, x * 2, M, K).cpu().numpy()
+    assert np.array_equal(a2, a * 2)
