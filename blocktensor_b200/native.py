@@ -82,6 +82,7 @@ SIGNATURES = {
     "bt_cuda_gemv_q8": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp]),
     "bt_cuda_pack_q8_units": (_i32, [_vp, _vp, _u32, _u32, _vp]),
     "bt_cuda_gemv_q8_units": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp]),
+    "bt_cuda_gemv_q8_units_noalloc": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp]),
     "bt_cuda_rmsnorm": (_i32, [_vp, _vp, _vp, _u32, _u32, _f32, _vp]),
     "bt_cuda_rope": (_i32, [_vp, _vp, _u32, _u32, _u32, _u32, _f32, _vp]),
     "bt_cuda_softmax": (_i32, [_vp, _vp, _u32, _u32, _vp]),

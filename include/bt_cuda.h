@@ -152,6 +152,25 @@ BT_API int bt_cuda_pack_q8_units(const void* W_blocks, void* units, uint32_t M, 
 BT_API int bt_cuda_gemv_q8_units(const void* units, const float* x, float* y, uint32_t M, uint32_t K,
                                  void* stream);
 
+/* bt_cuda_gemv_q8_units for callers that cannot allocate device memory (no
+ * counterpart in the reference).  An engine that reserves all device memory up
+ * front in its own pool, a runtime whose allocator must account for every
+ * byte, or a decode loop that must never hit cudaMalloc's implicit device
+ * synchronisation cannot let the library cudaMalloc a workspace on first use.
+ * This variant calls no cudaMalloc, cudaFree or allocating library routine: its
+ * scratch (partial sums of row groups split between CTAs, arrival tickets, a
+ * timeout flag) is a fixed 288 KB device array inside the library, held by
+ * every GPU that loads the library until the process exits.  Limits: M <=
+ * 1048576 rows, K <= 49152, at most 256 SMs; larger sizes return
+ * BT_ERR_INVALID_ARGUMENT.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress, with that device current); make that
+ * first call before any stream capture.  Every call on a device shares the one
+ * array and each call clears its tickets first, so calls that overlap on the
+ * GPU (concurrent streams) race and must be serialised by the caller.  Same
+ * inputs, outputs, alignment and arithmetic as bt_cuda_gemv_q8_units. */
+BT_API int bt_cuda_gemv_q8_units_noalloc(const void* units, const float* x, float* y, uint32_t M, uint32_t K,
+                                         void* stream);
+
 /* Batched int8 GEMV on the device layout: Y[b][m] = sum_k W[m][k] X[b][k],
  * b < B, for the dequant-GEMV microbenchmark.  B = 1 is the
  * reference's matvec_q8_0 (quant_types.cpp:101-121) on repacked weights. */
