@@ -102,8 +102,8 @@ def repack_q8_0(blocks, M: int, K: int, stream=None):
 
 
 def unit_bytes(M: int, K: int) -> int:
-    """Bytes of an M x K matrix in the tensor-core unit layout."""
-    return (M + 15) // 16 * (K // Q8_BLOCK) * 576
+    """Bytes of an M x K matrix in the tensor-core tile layout (128 x 32 tiles of 4608 bytes)."""
+    return (M + 127) // 128 * (K // Q8_BLOCK) * 4608
 
 
 def pack_q8_units(blocks, M: int, K: int, stream=None):

@@ -27,15 +27,11 @@
 #include <string>
 #include <vector>
 
-namespace bt {
-
-}  // namespace bt
-
 using namespace bt;
 
 // ---------------------------------------------------------------- engine objects
 
-// Matrices in the 576-byte unit layout of bt_gemv_mma.cuh (rows padded to 16).
+// Matrices in the 4608-byte tile layout of bt_gemv_mma.cuh (rows padded to 128).
 struct LayerDev {
     uint8_t* qkv;   // [D + 2 KVD] x D, q and k rows as RoPE pairs (i, i + hd/2) of each head
     uint8_t* o;     // D x D
@@ -60,7 +56,7 @@ struct bt_engine {
     float* embed = nullptr;
     float* out_norm = nullptr;
     uint8_t* head = nullptr;  // V x D units
-    // partial sums of row groups cut between two CTAs of a GEMV ([num_sms][32] + tickets)
+    // partial sums of row tiles cut between CTAs of a GEMV ([num_sms][2][128]) + one ticket per row tile
     float* split_part = nullptr;
     uint32_t* split_ticket = nullptr;
     // activations
@@ -134,7 +130,6 @@ int dev_alloc(std::vector<void*>& list, T** out, size_t count, const char* what)
     } while (0)
 
 uint32_t kvd(const bt_model_config& c) { return c.num_kv_heads * c.head_dim; }
-uint32_t pad16(uint32_t m) { return (m + 15) / 16 * 16; }
 
 int validate_config(const bt_model_config& c) {
     if (c.vocab_size == 0 || c.dim == 0 || c.hidden_dim == 0 || c.num_layers == 0 || c.num_heads == 0 ||
@@ -177,7 +172,7 @@ Slot layer_slot(bt_engine* e, uint32_t l, int j) {
     }
 }
 
-// Unit-layout matrix of M x K rows (padding rows zero).
+// Tile-layout matrix of M x K rows (padding rows zero).
 int alloc_units(bt_engine* e, uint8_t** out, uint32_t M, uint32_t K, const char* what) {
     const uint64_t bytes = unit_bytes(M, K);
     int rc = dev_alloc(e->allocs, out, bytes, what);
@@ -215,9 +210,14 @@ int alloc_weights(bt_engine* e) {
     BT_TRY_ALLOC(A, &e->am_idx, nblk, "argmax idx");
     BT_TRY_ALLOC(A, &e->am_ticket, 4, "argmax ticket");
     BT_CUDA_CHECK(cudaMemsetAsync(e->am_ticket, 0, 16, e->stream));
-    BT_TRY_ALLOC(A, &e->split_part, (size_t)e->num_sms * 32, "split partials");
-    BT_TRY_ALLOC(A, &e->split_ticket, (size_t)e->num_sms, "split tickets");
-    BT_CUDA_CHECK(cudaMemsetAsync(e->split_ticket, 0, sizeof(uint32_t) * e->num_sms, e->stream));
+    // split scratch of the GEMVs: partials [SM][2][128], one ticket per row tile of the tallest matrix
+    uint32_t rows = (uint32_t)V;
+    if (2 * F > rows) rows = (uint32_t)(2 * F);
+    if (D + 2 * KV > rows) rows = (uint32_t)(D + 2 * KV);
+    const size_t tickets = mma_row_tiles(unit_rows(rows));
+    BT_TRY_ALLOC(A, &e->split_part, (size_t)e->num_sms * 2 * kTileRows, "split partials");
+    BT_TRY_ALLOC(A, &e->split_ticket, tickets, "split tickets");
+    BT_CUDA_CHECK(cudaMemsetAsync(e->split_ticket, 0, sizeof(uint32_t) * tickets, e->stream));
     return BT_OK;
 }
 
@@ -260,7 +260,7 @@ int enqueue_step(bt_engine* e, bt_kv* kv, cudaStream_t s, Marks* marks = nullptr
     const uint32_t QKV = D + 2 * KV;
     // the GEMV that follows each one, for the producer's L2 prefetch
     auto next = [&](const uint8_t* u, uint32_t M, uint32_t K) {
-        return e->prefetch_bytes ? NextW{u, pad16(M), K, mma_grid(pad16(M), nsm), e->prefetch_bytes}
+        return e->prefetch_bytes ? NextW{u, unit_rows(M), K, mma_grid(unit_rows(M), K, nsm), e->prefetch_bytes}
                                  : NextW{nullptr, 0, 0, 0, 0};
     };
     uint32_t* errp = &kv->st->error;
@@ -273,7 +273,7 @@ int enqueue_step(bt_engine* e, bt_kv* kv, cudaStream_t s, Marks* marks = nullptr
         char* vl = static_cast<char*>(kv->v) + l * kv_layer * esz;
         // qkv
         {
-            const UnitW w{L.qkv, QKV, pad16(QKV), D};
+            const UnitW w{L.qkv, QKV, unit_rows(QKV), D};
             const NextW nx = next(L.o, D, D);
             MProNorm pro{e->x, L.attn_norm, c.rms_norm_eps, l == 0 ? e->embed : nullptr, kv->st, e->x};
             cudaError_t err;
@@ -299,11 +299,11 @@ int enqueue_step(bt_engine* e, bt_kv* kv, cudaStream_t s, Marks* marks = nullptr
             BT_MARK();
         }
         // o-proj + residual
-        BT_CUDA_CHECK(launch_gemv_mma(UnitW{L.o, D, pad16(D), D}, MProCopy{e->attn}, SEpiResidual{e->x, nullptr}, sp,
+        BT_CUDA_CHECK(launch_gemv_mma(UnitW{L.o, D, unit_rows(D), D}, MProCopy{e->attn}, SEpiResidual{e->x, nullptr}, sp,
                                       errp, nsm, s, pdl, next(L.gu, 2 * F, D)));
         BT_MARK();
         // gate/up + SwiGLU
-        BT_CUDA_CHECK(launch_gemv_mma(UnitW{L.gu, 2 * F, pad16(2 * F), D},
+        BT_CUDA_CHECK(launch_gemv_mma(UnitW{L.gu, 2 * F, unit_rows(2 * F), D},
                                       MProNorm{e->x, L.ffn_norm, c.rms_norm_eps, nullptr, nullptr, nullptr},
                                       SEpiSwiGLU{e->act}, sp, errp, nsm, s, pdl, next(L.d, D, F)));
         BT_MARK();
@@ -311,14 +311,14 @@ int enqueue_step(bt_engine* e, bt_kv* kv, cudaStream_t s, Marks* marks = nullptr
         {
             float* tap = e->taps_on ? e->taps + (size_t)l * D : nullptr;
             const NextW nx = l + 1 < c.num_layers ? next(e->layers[l + 1].qkv, QKV, D) : next(e->head, c.vocab_size, D);
-            BT_CUDA_CHECK(launch_gemv_mma(UnitW{L.d, D, pad16(D), F}, MProCopy{e->act}, SEpiResidual{e->x, tap}, sp,
+            BT_CUDA_CHECK(launch_gemv_mma(UnitW{L.d, D, unit_rows(D), F}, MProCopy{e->act}, SEpiResidual{e->x, tap}, sp,
                                           errp, nsm, s, pdl, nx));
             BT_MARK();
         }
     }
     {
         EpiLogits epi{e->logits, e->am_val, e->am_idx, e->am_ticket, kv->st, kv->tok_hist, kv->max_seq};
-        BT_CUDA_CHECK(launch_gemv_mma(UnitW{e->head, c.vocab_size, pad16(c.vocab_size), D},
+        BT_CUDA_CHECK(launch_gemv_mma(UnitW{e->head, c.vocab_size, unit_rows(c.vocab_size), D},
                                       MProNorm{e->x, e->out_norm, c.rms_norm_eps, nullptr, nullptr, nullptr},
                                       SEpiLogits{epi}, sp, errp, nsm, s, pdl, next(e->layers[0].qkv, QKV, D)));
         BT_MARK();

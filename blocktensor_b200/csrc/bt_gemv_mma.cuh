@@ -1,33 +1,40 @@
-// bt_gemv_mma.cuh -- batch-1 int8 GEMV on the tensor cores, stream-K over HBM.
+// bt_gemv_mma.cuh -- batch-1 int8 GEMV on the 5th-generation tensor cores.
 //
 // Arithmetic.  The reference computes y[r] = sum_b scale[r][b] * sum_{i<32}
 // q[r][32b+i] * x[32b+i] in fp32 (quantization/quant_types.cpp:101-121).  Here
 // x is first written as a 22-bit fixed-point vector v = round(x * 2^e) with one
-// power-of-two exponent e per vector (|v| < 2^22), and v as three signed
-// base-256 digits hi/mid/lo (|hi| <= 64).  One mma.sync.m16n8k32 s8*s8->s32
-// per (16 rows, 32 columns) gives, for every row, the three digit dot products
-// sum_i q_i * digit_i exactly in integers; they are combined in fp32
-// ((256*hi + mid)*256 + lo), scaled by the block scale and accumulated in fp32
-// across blocks, and 2^-e is applied at the end.  The only rounding besides fp32
-// accumulation is x's quantisation step of 2^-21 relative to max|x|.
+// power-of-two exponent e per vector (|v| <= 2^21), and v as three signed
+// base-256 digits hi/mid/lo.  One tcgen05.mma (kind::i8, M=128, N=8, K=32) per
+// 128-row x 32-column tile gives, for every row, the three digit dot products
+// sum_i q_i * digit_i exactly as int32 in tensor memory; they are combined in
+// fp32 ((256*hi + mid)*256 + lo), scaled by the block scale and accumulated in
+// fp32 across blocks, and 2^-e is applied at the end.  The only rounding
+// besides fp32 accumulation is x's quantisation step of 2^-21 relative to
+// max|x|.
 //
-// Layout (written by the repack kernel): rows in groups of 16, each group as
-// K/32 units of 576 bytes: the 16x32 int8 block in mma fragment order (lane t's
-// 16 bytes = its four A registers) followed by the 16 fp32 block scales in
-// row order 0, 8, 1, 9, ..., 7, 15 (the two rows a lane pair finishes are
-// adjacent).  A matrix is one contiguous stream of units, group-major.
+// Layout (written by the pack kernel): rows in tiles of 128; a matrix is the
+// stream of its (row tile, 32-column block) tiles, row-tile-major.  A tile is
+// 4608 bytes: the 128x32 int8 block in the UMMA K-major no-swizzle canonical
+// layout (core matrix of 8 rows x 16 bytes = 128 contiguous bytes; core
+// matrices of the two 16-byte K halves 128 bytes apart, 8-row groups 256
+// bytes apart), then the 128 fp32 block scales in row order.
 //
-// Work split (stream-K).  CTA c of G owns units [U c/G, U (c+1)/G): every CTA
-// moves the same number of bytes, whatever M.  A 16-row group cut between two
-// CTAs is finished by the one that completes second, adding the two partial
-// sums in a fixed order (lower columns first), so results are deterministic.
+// Work split (stream-K).  CTA c of G owns tiles [U c/G, U (c+1)/G): every CTA
+// moves the same number of bytes, whatever M.  A row tile cut between several
+// CTAs is finished by the one that completes last, adding the CTAs' partial
+// sums in CTA order, so results are deterministic.
 //
-// Warp roles (320 threads): warps 0-7 consume, warp 8 produces (cp.async.bulk
-// of 32-unit stages into an mbarrier ring; it never waits for the previous
-// kernel, so under programmatic dependent launch the ring fills while the
-// previous kernel drains), warp 9 runs the epilogue of each finished group.
-// All waits are bounded (2 s); an expired wait sets *err and the CTA still
-// finishes (consumers stop waiting but keep arriving on every barrier).
+// Warp roles (352 threads): warp 0 produces (cp.async.bulk of 4-tile stages
+// into an mbarrier ring; weights never depend on the previous kernel, so under
+// programmatic dependent launch the ring fills while the previous kernel
+// drains); warp 1 owns the tensor memory and one of its lanes issues the MMAs;
+// warps 2-9 read the digit sums from tensor memory (warp w reads TMEM lanes
+// 32 (w%4) .. +31, the two warps of a lane quarter take alternate tile pairs)
+// and accumulate; warp 10 finishes each row tile (cross-CTA merge, epilogue).
+// Warps 1-10 build the digits first.  No thread loads weights into registers:
+// the tensor cores read them from the ring, which leaves the SM's shared
+// memory path to the bulk copies.  All waits are bounded (2 s); an expired wait
+// sets *err and the CTA still finishes and frees its tensor memory.
 #pragma once
 
 #include "bt_common.cuh"
@@ -36,27 +43,38 @@
 
 namespace bt {
 
-constexpr uint32_t kUnitRows = 16;
-constexpr uint32_t kUnitK = 32;
-constexpr uint32_t kUnitQBytes = 512;   // 16 x 32 int8
-constexpr uint32_t kUnitBytes = 576;    // + 16 fp32 scales
-constexpr int kMmaConsumers = 8;
-constexpr int kMmaProducerWarp = 8;
-constexpr int kMmaEpilogueWarp = 9;
-constexpr int kMmaThreads = 320;
-constexpr int kMmaRedSlots = 8;
-constexpr uint32_t kMmaMaxRing = 16;
-constexpr uint32_t kMmaStageUnits = 32;  // 18 KB stages
+constexpr uint32_t kTileRows = 128;
+constexpr uint32_t kTileK = 32;
+constexpr uint32_t kTileQBytes = 4096;   // 128 x 32 int8
+constexpr uint32_t kTileBytes = 4608;    // + 128 fp32 scales
+constexpr uint32_t kStageTiles = 4;      // 18 KB stages
+constexpr uint32_t kStageBytes = kStageTiles * kTileBytes;
+constexpr uint32_t kTileCols = 8;        // TMEM columns per tile (N = 8)
+constexpr int kMmaThreads = 352;
+constexpr int kProducerWarp = 0;
+constexpr int kMmaWarp = 1;
+constexpr int kAccWarp0 = 2;             // accumulator warps 2..9
+constexpr int kAccWarps = 8;
+constexpr int kFinWarp = 10;
+constexpr int kDigitThreads = 320;       // warps 1..10
+constexpr int kRedSlots = 4;
+constexpr uint32_t kMmaMaxRing = 16;     // stages (16 x 32 TMEM columns = 512)
 
-// A matrix in the unit layout.
+// Instruction descriptor: D s32, A and B s8, both K-major, N = 8, M = 128.
+constexpr uint32_t kIdescS8 = (2u << 4) | (1u << 7) | (1u << 10) | ((8u >> 3) << 17) | ((128u >> 4) << 24);
+
+inline __host__ __device__ uint32_t unit_rows(uint32_t M) { return (M + kTileRows - 1) / kTileRows * kTileRows; }
+
+// A matrix in the tile layout.
 struct UnitW {
-    const uint8_t* units;  // [Mp/16][K/32][576]
+    const uint8_t* units;  // [Mp/128][K/32][4608]
     uint32_t M;            // rows the epilogue writes
-    uint32_t Mp;           // rows in the layout (multiple of 16)
+    uint32_t Mp;           // rows in the layout (multiple of 128)
     uint32_t K;            // multiple of 32
 };
 
-// Partial sums of 16-row groups cut between CTA c and c+1: part[c][side][16], ticket[c].
+// Partial sums of row tiles cut between CTAs: part[cta][side][128] (side 0 =
+// the CTA's first row tile, 1 = its last), ticket[row tile] counts the pieces.
 struct SplitScratch {
     float* part;
     uint32_t* ticket;
@@ -64,7 +82,8 @@ struct SplitScratch {
 
 struct MmaShape {
     uint32_t NS;           // ring stages
-    uint32_t stage_bytes;  // kMmaStageUnits * kUnitBytes
+    uint32_t xstride;      // bytes between the two digit arrays (K halves)
+    uint32_t tmem_cols;    // power of two >= 32 * NS
 };
 
 // ---------------------------------------------------------------- prologues
@@ -119,10 +138,16 @@ __device__ __forceinline__ void digits3(int v, int& hi, int& mid, int& lo) {
     hi = (v1 - mid) >> 8;
 }
 
-// Writes the mma B fragments of one item: 8 elements (block blk, lanes tig of
-// each digit) as xf[blk][digit * 4 + tig].
-__device__ __forceinline__ void pack_item(uint2* xf, uint32_t idx, const float4& a, const float4& b, float c1,
-                                          float c2) {
+// Digit arrays of the B operand: for each K half c (0, 1), block b's three
+// digit rows (hi, mid, lo; 16 bytes each = the 16 elements of that half) at
+// xb + c * xstride + 48 b.  The B tile of block b (N = 8 rows of 16 bytes per
+// K half) starts at its hi row: rows 3..7 are the next blocks' digits, which
+// only reach D columns 3..7, never read.  128 bytes of padding end each array.
+
+// Writes the digits of one item (8 elements: block idx/4, elements 4 (idx%4)
+// + {0..3} of each K half).
+__device__ __forceinline__ void pack_item(uint8_t* xb, uint32_t xstride, uint32_t idx, const float4& a,
+                                          const float4& b, float c1, float c2) {
     const float va[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     uint32_t r[3][2] = {{0, 0}, {0, 0}, {0, 0}};
 #pragma unroll
@@ -137,45 +162,48 @@ __device__ __forceinline__ void pack_item(uint2* xf, uint32_t idx, const float4&
     }
     const uint32_t blk = idx >> 2, tig = idx & 3;
 #pragma unroll
-    for (int p = 0; p < 3; ++p) xf[blk * 12 + p * 4 + tig] = make_uint2(r[p][0], r[p][1]);
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int d = 0; d < 3; ++d)
+            *reinterpret_cast<uint32_t*>(xb + c * xstride + blk * 48 + d * 16 + tig * 4) = r[d][c];
 }
 
-// Builds xf[b][lane] (lane < 12: digit lane/4 of the 8 elements that mma B
-// fragment lane holds) and returns the exponent e; *bad when the vector holds
-// an inf or NaN (the outputs are then NaN).  One global round trip: item idx
-// (block idx/4, lane tig = idx%4, elements 32 b + 4 tig + {0..3, 16..19}) is
-// loaded once into registers by consumer thread idx % 256 (K <= 12288; larger
-// vectors load their tail twice).  Consumer threads only.
+// Builds the digit arrays and returns the exponent e; *bad when the vector
+// holds an inf or NaN (the outputs are then NaN).  One global round trip: item
+// idx is loaded once into registers by digit thread idx % 320 (K <= 12800;
+// larger vectors load their tail twice).  Called by the 320 threads of warps
+// 1-10 (tid = 0..319); ends with the digits visible to the tensor cores.
 template <class Pro>
-__device__ int build_digits(const Pro& pro, uint32_t K, uint2* xf, float* red, bool& bad) {
-    constexpr int R = 6;
+__device__ int build_digits(const Pro& pro, uint32_t K, uint8_t* xb, uint32_t xstride, float* red, uint32_t tid,
+                            bool& bad) {
+    constexpr int R = 5;
     const float* s = pro.base(K);
     const uint32_t items = K >> 3;
     float ss = 0.0f, mx = 0.0f;
     float4 pa[R], pb[R];
 #pragma unroll
     for (int i = 0; i < R; ++i) {
-        const uint32_t idx = threadIdx.x + 256u * i;
+        const uint32_t idx = tid + kDigitThreads * i;
         if (idx < items) {
             const uint32_t k = (idx >> 2) * 32 + (idx & 3) * 4;
             pa[i] = pro.load(s, k, ss, mx);
             pb[i] = pro.load(s, k + 16, ss, mx);
         }
     }
-    for (uint32_t idx = threadIdx.x + 256u * R; idx < items; idx += 256) {
+    for (uint32_t idx = tid + kDigitThreads * R; idx < items; idx += kDigitThreads) {
         const uint32_t k = (idx >> 2) * 32 + (idx & 3) * 4;
         pro.load(s, k, ss, mx);
         pro.load(s, k + 16, ss, mx);
     }
-    // sum and max over the 256 consumers
+    // sum and max over the 10 warps
     ss = warp_sum(ss);
     mx = warp_max(mx);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (lane == 0) { red[warp] = ss; red[8 + warp] = mx; }
-    consumer_sync();
+    const uint32_t lane = tid & 31, w = tid >> 5;
+    if (lane == 0) { red[w] = ss; red[10 + w] = mx; }
+    digit_sync();
     float tss = 0.0f, tmx = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) { tss += red[i]; tmx = fmaxf(tmx, red[8 + i]); }
+    for (int i = 0; i < 10; ++i) { tss += red[i]; tmx = fmaxf(tmx, red[10 + i]); }
     const float f = pro.factor(tss, K);
     const float m = tmx * f;
     // m * 2^e in [2^20, 2^21): values round to |v| <= 2^21 (slack for the rounding of m)
@@ -190,22 +218,23 @@ __device__ int build_digits(const Pro& pro, uint32_t K, uint2* xf, float* red, b
     const float c1 = ldexpf(1.0f, e / 2), c2 = ldexpf(f, e - e / 2);
 #pragma unroll
     for (int i = 0; i < R; ++i) {
-        const uint32_t idx = threadIdx.x + 256u * i;
-        if (idx < items) pack_item(xf, idx, pa[i], pb[i], c1, c2);
+        const uint32_t idx = tid + kDigitThreads * i;
+        if (idx < items) pack_item(xb, xstride, idx, pa[i], pb[i], c1, c2);
     }
-    for (uint32_t idx = threadIdx.x + 256u * R; idx < items; idx += 256) {
+    for (uint32_t idx = tid + kDigitThreads * R; idx < items; idx += kDigitThreads) {
         const uint32_t k = (idx >> 2) * 32 + (idx & 3) * 4;
         float d0 = 0.0f, d1 = 0.0f;
         const float4 a = pro.load(s, k, d0, d1), b = pro.load(s, k + 16, d0, d1);
-        pack_item(xf, idx, a, b, c1, c2);
+        pack_item(xb, xstride, idx, a, b, c1, c2);
     }
-    consumer_sync();
+    fence_proxy_async();  // generic-proxy writes -> visible to the tensor cores
+    digit_sync();
     return e;
 }
 
 // ---------------------------------------------------------------- epilogues (epilogue warp)
-// tile(): the 32 lanes of the epilogue warp, once per finished 16-row group;
-// rs(t) is the final value of row row0 + t.  end(): after the CTA's last group.
+// tile(): the 32 lanes of the finisher warp, once per finished row tile;
+// rs(t) is the final value of row row0 + t.  end(): after the CTA's last tile.
 
 struct StreamState {
     float bv;     // running argmax value of this lane (logits epilogue)
@@ -345,74 +374,85 @@ struct SEpiLogits {
 
 // ---------------------------------------------------------------- kernel
 
-// The next GEMV of the sequence: this CTA prefetches into L2 the first bytes
-// of the unit range that CTA blockIdx.x of that GEMV will stream, so its first
-// stages hit in L2 while this kernel drains.
+// The next GEMV of the sequence: the producer prefetches into L2 the first
+// bytes of the tile range that CTA blockIdx.x of that GEMV will stream, so its
+// first stages hit in L2 while this kernel drains.
 struct NextW {
     const uint8_t* units;  // null: nothing to prefetch
     uint32_t Mp, K, grid;
     uint32_t bytes;        // prefetch budget per CTA
 };
 
+// CTA of a G-way split of U tiles that owns tile u: the largest c with U c / G <= u.
+__device__ __forceinline__ uint32_t split_cta(uint64_t u, uint64_t U, uint32_t G) {
+    return (uint32_t)(((u + 1) * G + U - 1) / U) - 1;
+}
+
 template <class Pro, class Epi>
 __global__ void __launch_bounds__(kMmaThreads, 2)
 gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW nx, uint32_t* err) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t full[kMmaMaxRing], empty[kMmaMaxRing];
-    __shared__ __align__(8) uint64_t red_full[kMmaRedSlots], red_free[kMmaRedSlots];
-    __shared__ float red[kMmaRedSlots][kMmaConsumers][16];
-    __shared__ float fin[16];
-    __shared__ float red32[32];
-    __shared__ int s_e;
-    __shared__ bool s_bad;
+    __shared__ __align__(8) uint64_t full[kMmaMaxRing], empty[kMmaMaxRing], mma_done[kMmaMaxRing];
+    __shared__ __align__(8) uint64_t red_full[kRedSlots], red_free[kRedSlots];
+    __shared__ float red[kRedSlots][2][kTileRows];
+    __shared__ float fin[kTileRows];
+    __shared__ float red20[20];
+    __shared__ uint32_t s_tmem;
 
     pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t K = W.K, NB = K / kUnitK, NS = sh.NS;
-    const uint32_t U = (W.Mp / kUnitRows) * NB;
+    const uint32_t K = W.K, NB = K / kTileK, NS = sh.NS;
+    const uint32_t U = (W.Mp / kTileRows) * NB;
     const uint32_t G = gridDim.x, c = blockIdx.x;
     const uint32_t u0 = (uint32_t)(((uint64_t)U * c) / G);
     const uint32_t u1 = (uint32_t)(((uint64_t)U * (c + 1)) / G);
     const uint32_t g_first = u0 / NB, g_last = (u1 - 1) / NB;
     const uint32_t ngroups = g_last - g_first + 1;
-    const uint32_t nstages = (u1 - u0 + kMmaStageUnits - 1) / kMmaStageUnits;
+    const uint32_t nstages = (u1 - u0 + kStageTiles - 1) / kStageTiles;
     uint8_t* ring = smem;
-    uint2* xf = reinterpret_cast<uint2*>(smem + (size_t)NS * sh.stage_bytes);
+    uint8_t* xb = smem + (size_t)NS * kStageBytes;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kMmaConsumers);
+            mbar_init(&empty[s], kAccWarps);
+            mbar_init(&mma_done[s], 1);
         }
-        for (int r = 0; r < kMmaRedSlots; ++r) {
-            mbar_init(&red_full[r], kMmaConsumers);
+        for (int r = 0; r < kRedSlots; ++r) {
+            mbar_init(&red_full[r], kAccWarps);
             mbar_init(&red_free[r], 1);
         }
         fence_mbar_init();
     }
+    if (warp == kMmaWarp) {
+        tmem_alloc(&s_tmem, sh.tmem_cols);
+        tmem_relinquish();
+    }
+    tcgen05_fence_before();
     __syncthreads();
+    tcgen05_fence_after();
+    const uint32_t tmem = s_tmem;
 
-    if (warp == kMmaProducerWarp) {
-        // ---------------- producer: weights never depend on the previous kernel
+    if (warp == kProducerWarp) {
+        // ---------------- producer
         if (lane == 0) {
             uint32_t issued = 0, s = 0, ph = 0;
             for (uint32_t j = 0; j < nstages; ++j) {
                 if (j >= NS && !mbar_wait(&empty[s], ph ^ 1, err)) break;
-                const uint32_t ub = u0 + j * kMmaStageUnits;
-                const uint32_t n = min(kMmaStageUnits, u1 - ub);
-                mbar_expect_tx(&full[s], n * kUnitBytes);
-                bulk_g2s(ring + (size_t)s * sh.stage_bytes, W.units + (size_t)ub * kUnitBytes, n * kUnitBytes, &full[s]);
+                const uint32_t ub = u0 + j * kStageTiles;
+                const uint32_t n = min(kStageTiles, u1 - ub);
+                mbar_expect_tx(&full[s], n * kTileBytes);
+                bulk_g2s(ring + (size_t)s * kStageBytes, W.units + (size_t)ub * kTileBytes, n * kTileBytes, &full[s]);
                 issued = j + 1;
                 if (++s == NS) { s = 0; ph ^= 1; }
             }
             // warm L2 with the start of this CTA's share of the next GEMV
             if (nx.units && c < nx.grid) {
-                const uint32_t nb2 = nx.K / kUnitK;
-                const uint64_t U2 = (uint64_t)(nx.Mp / kUnitRows) * nb2;
+                const uint64_t U2 = (uint64_t)(nx.Mp / kTileRows) * (nx.K / kTileK);
                 const uint64_t v0 = U2 * c / nx.grid, v1 = U2 * (c + 1) / nx.grid;
-                uint64_t bytes = (v1 - v0) * kUnitBytes;
+                uint64_t bytes = (v1 - v0) * kTileBytes;
                 if (bytes > nx.bytes) bytes = nx.bytes;
-                const uint8_t* p = nx.units + v0 * kUnitBytes;
+                const uint8_t* p = nx.units + v0 * kTileBytes;
                 for (uint64_t o = 0; o < bytes; o += 32768) {
                     const uint32_t n = (uint32_t)((bytes - o) < 32768 ? (bytes - o) : 32768);
                     bulk_prefetch_l2(p + o, n & ~15u);
@@ -425,147 +465,176 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
         return;
     }
 
-    if (warp == kMmaEpilogueWarp) {
-        // ---------------- epilogue: finished groups, cross-CTA merge of cut groups
-        pdl_wait();
+    // ---------------- warps 1-10: the input vector's digits (every thread gets e and bad)
+    pdl_wait();
+    bool bad = false;
+    const int e = build_digits(pro, K, xb, sh.xstride, red20, threadIdx.x - 32, bad);
+
+    if (warp == kMmaWarp) {
+        // ---------------- MMA issue (one lane), then tensor memory release
+        if (lane == 0) {
+            bool ok = true;
+            uint32_t s = 0, ph = 0, b = u0 % NB;
+            const uint32_t xaddr = smem_u32(xb);
+            for (uint32_t j = 0; j < nstages; ++j) {
+                if (ok) ok = mbar_wait(&full[s], ph, err);
+                tcgen05_fence_after();
+                const uint32_t n = min(kStageTiles, u1 - (u0 + j * kStageTiles));
+                const uint32_t abase = smem_u32(ring + (size_t)s * kStageBytes);
+                for (uint32_t t = 0; t < n; ++t) {
+                    if (ok) {
+                        const uint64_t ad = umma_desc(abase + t * kTileBytes, 128, 256);
+                        const uint64_t bd = umma_desc(xaddr + b * 48, sh.xstride, 128);
+                        umma_s8(tmem + s * (kStageTiles * kTileCols) + t * kTileCols, ad, bd, kIdescS8, 0);
+                    }
+                    if (++b == NB) b = 0;
+                }
+                umma_commit(&mma_done[s]);  // arrives once the stage's MMAs are complete
+                if (++s == NS) { s = 0; ph ^= 1; }
+            }
+        }
+        __syncwarp();
+        tmem_sync();  // every accumulator warp is done with tensor memory
+        tcgen05_fence_after();
+        tmem_dealloc(tmem, sh.tmem_cols);
+        return;
+    }
+
+    if (warp == kFinWarp) {
+        // ---------------- finisher: sum the two halves, cross-CTA merge, epilogue
         StreamState est{-INFINITY, 0xFFFFFFFFu};
         bool ok = true;
-        const bool hi_cut = (u0 % NB) != 0;   // g_first began in CTA c-1
-        const bool lo_cut = (u1 % NB) != 0;   // g_last continues in CTA c+1
         uint32_t slot = 0, ph = 0;
         for (uint32_t gi = 0; gi < ngroups; ++gi) {
             if (ok) ok = mbar_wait(&red_full[slot], ph, err);
-            float v = 0.0f;
-            if (lane < 16) {
+            float v[4];
 #pragma unroll
-                for (int w = 0; w < kMmaConsumers; ++w) v += red[slot][w][lane];
-                v = s_bad ? __int_as_float(0x7fc00000) : ldexpf(v, -s_e);
+            for (int i = 0; i < 4; ++i) {
+                const int r = lane + 32 * i;
+                v[i] = bad ? __int_as_float(0x7fc00000) : ldexpf(red[slot][0][r] + red[slot][1][r], -e);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&red_free[slot]);
-            if (++slot == kMmaRedSlots) { slot = 0; ph ^= 1; }
-            const int side = (gi == 0 && hi_cut) ? 1 : ((gi == ngroups - 1 && lo_cut) ? 0 : -1);
-            if (side >= 0) {
-                const uint32_t bnd = side == 1 ? c - 1 : c;
-                float* part = sp.part + (size_t)bnd * 32;
-                if (lane < 16) part[side * 16 + lane] = v;
+            if (++slot == kRedSlots) { slot = 0; ph ^= 1; }
+            const uint32_t g = g_first + gi;
+            const uint32_t c_lo = split_cta((uint64_t)g * NB, U, G);
+            const uint32_t c_hi = split_cta((uint64_t)(g + 1) * NB - 1, U, G);
+            if (c_lo != c_hi) {
+                const uint32_t side = g == g_first ? 0 : 1;
+                float* part = sp.part + ((size_t)c * 2 + side) * kTileRows;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) part[lane + 32 * i] = v[i];
                 __threadfence();
                 __syncwarp();
-                uint32_t second = 0;
-                if (lane == 0) second = atomicAdd(sp.ticket + bnd, 1u);
-                second = __shfl_sync(0xffffffffu, second, 0);
-                if (!second) continue;  // the other CTA finishes this group
+                uint32_t last = 0;
+                if (lane == 0) last = atomicAdd(sp.ticket + g, 1u) == c_hi - c_lo;
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (!last) continue;  // a later CTA finishes this row tile
                 __threadfence();
-                if (lane < 16) v = __ldcg(part + lane) + __ldcg(part + 16 + lane);  // lower columns first
-                if (lane == 0) sp.ticket[bnd] = 0;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) v[i] = 0.0f;
+                for (uint32_t cc = c_lo; cc <= c_hi; ++cc) {  // fixed order: CTA index
+                    const uint32_t first_cc = (uint32_t)(((uint64_t)U * cc) / G) / NB;
+                    const float* pc = sp.part + ((size_t)cc * 2 + (g == first_cc ? 0 : 1)) * kTileRows;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) v[i] += __ldcg(pc + lane + 32 * i);
+                }
+                if (lane == 0) sp.ticket[g] = 0;
             }
-            if (lane < 16) fin[lane] = v;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) fin[lane + 32 * i] = v[i];
             __syncwarp();
-            epi.tile(est, (g_first + gi) * kUnitRows, kUnitRows, W.M, lane, [&](uint32_t t) { return fin[t]; });
+            epi.tile(est, g * kTileRows, kTileRows, W.M, lane, [&](uint32_t t) { return fin[t]; });
             __syncwarp();
         }
         epi.end(est, lane);
         return;
     }
 
-    // ---------------- consumers
-    pdl_wait();
-    bool bad = false;
-    const int e = build_digits(pro, K, xf, red32, bad);
-    if (threadIdx.x == 0) {
-        s_e = e;
-        s_bad = bad;
-    }
-
-    // C fragment: lane (grp, tig) holds rows grp and grp+8 at columns 2 tig, 2 tig+1,
-    // i.e. tig 0 the hi and mid sums, tig 1 the lo sums (tig 2, 3: zero columns).
-    // After one exchange, even lanes finish row grp and odd lanes row grp + 8.
-    const int grp = lane >> 2, odd = lane & 1;
-    const float mA = odd ? 1.0f : 256.0f;
-    const uint32_t soff = kUnitQBytes + (uint32_t)(grp * 2 + odd) * 4;  // scales stored as (r, r+8) pairs
+    // ---------------- accumulators: warp (quarter q, parity p) takes tiles 2p, 2p+1 of every stage
+    const uint32_t q = warp & 3, p = (warp - kAccWarp0) >> 2;
+    const uint32_t row = 32 * q + lane;
+    const uint32_t taddr = tmem + ((32 * q) << 16) + 16 * p;
     float acc = 0.0f;
     bool ok = true;
     uint32_t cur_g = g_first, rslot = 0, rph = 0, gi = 0;
     auto flush = [&]() {
-        if (gi >= kMmaRedSlots && ok) ok = mbar_wait(&red_free[rslot], rph ^ 1, err);
-        if ((lane & 3) < 2) red[rslot][warp][grp + 8 * odd] = acc;
+        if (gi >= kRedSlots && ok) ok = mbar_wait(&red_free[rslot], rph ^ 1, err);
+        red[rslot][p][row] = acc;
         __syncwarp();
         if (lane == 0) mbar_arrive(&red_full[rslot]);
         acc = 0.0f;
         ++gi;
-        if (++rslot == kMmaRedSlots) { rslot = 0; rph ^= 1; }
+        if (++rslot == kRedSlots) { rslot = 0; rph ^= 1; }
         ++cur_g;
     };
-
-    // warp w takes the 4 consecutive units 4w..4w+3 of every stage
-    constexpr int kPerWarp = kMmaStageUnits / kMmaConsumers;
-    uint32_t g = (u0 + kPerWarp * warp) / NB;            // group and block of the warp's next unit
-    uint32_t b = (u0 + kPerWarp * warp) - g * NB;
+    uint32_t g = (u0 + 2 * p) / NB;             // row tile and block of the warp's first tile
+    uint32_t b = (u0 + 2 * p) - g * NB;
     uint32_t s = 0, ph = 0;
     for (uint32_t j = 0; j < nstages; ++j) {
-        if (ok) ok = mbar_wait(&full[s], ph, err);
-        const uint32_t n = min(kMmaStageUnits, u1 - (u0 + j * kMmaStageUnits));
-        const uint8_t* wb = ring + (size_t)s * sh.stage_bytes + (size_t)(kPerWarp * warp) * kUnitBytes;
-        float y[kPerWarp], sc[kPerWarp];
-        uint32_t gq[kPerWarp];
+        if (ok) ok = mbar_wait(&mma_done[s], ph, err);
+        tcgen05_fence_after();
+        uint32_t d[16];
+        tmem_ld16(taddr + s * (kStageTiles * kTileCols), d);
+        const uint32_t n = min(kStageTiles, u1 - (u0 + j * kStageTiles));
+        const uint8_t* st = ring + (size_t)s * kStageBytes + kTileQBytes + row * 4;
+        const float sc0 = 2 * p < n ? *reinterpret_cast<const float*>(st + (2 * p) * kTileBytes) : 0.0f;
+        const float sc1 = 2 * p + 1 < n ? *reinterpret_cast<const float*>(st + (2 * p + 1) * kTileBytes) : 0.0f;
+        tmem_wait_ld();
+        tcgen05_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);  // stage (smem and TMEM columns) free
+        if (++s == NS) { s = 0; ph ^= 1; }
 #pragma unroll
-        for (int q = 0; q < kPerWarp; ++q) {
-            gq[q] = g;
-            y[q] = sc[q] = 0.0f;
-            if ((uint32_t)(kPerWarp * warp + q) < n) {
-                const uint8_t* up = wb + q * kUnitBytes;
-                const uint4 a = *reinterpret_cast<const uint4*>(up + lane * 16);
-                const uint2 bx = lane < 12 ? xf[b * 12 + lane] : make_uint2(0u, 0u);
-                int d0, d1, d2, d3;
-                mma_s8_16832(a, bx, d0, d1, d2, d3);
-                const float fa = fmaf(small_i2f(d0), mA, small_i2f(d1));  // even: 256 hi + mid, odd: lo
-                const float fb = fmaf(small_i2f(d2), mA, small_i2f(d3));
-                const float r = __shfl_xor_sync(0xffffffffu, odd ? fa : fb, 1);
-                y[q] = fmaf(odd ? r : fa, 256.0f, odd ? fb : r);
-                sc[q] = *reinterpret_cast<const float*>(up + soff);
+        for (int t = 0; t < 2; ++t) {
+            if (2 * p + t < n) {
+                while (cur_g < g) flush();
+                const uint32_t* dt = d + 8 * t;  // columns hi, mid, lo of this tile
+                const float y = fmaf(fmaf(small_i2f((int)dt[0]), 256.0f, small_i2f((int)dt[1])), 256.0f,
+                                     small_i2f((int)dt[2]));
+                acc = fmaf(t ? sc1 : sc0, y, acc);
             }
             if (++b == NB) { b = 0; ++g; }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);  // slot free for the producer
-        if (++s == NS) { s = 0; ph ^= 1; }
-#pragma unroll
-        for (int q = 0; q < kPerWarp; ++q) {
-            if ((uint32_t)(kPerWarp * warp + q) >= n) break;
-            while (cur_g < gq[q]) flush();
-            acc = fmaf(sc[q], y[q], acc);
-        }
-        b += kMmaStageUnits - kPerWarp;  // the other warps' units of the stage
+        b += kStageTiles - 2;  // the other parity's tiles of the stage
         while (b >= NB) { b -= NB; ++g; }
     }
     while (cur_g <= g_last) flush();
+    tcgen05_fence_before();
+    tmem_sync();
 }
 
 // ---------------------------------------------------------------- host side
 
+inline uint32_t mma_xstride(uint32_t K) { return ((K / 32) * 48 + 128 + 15) & ~15u; }
+
 inline size_t mma_smem(const MmaShape& sh, uint32_t K) {
-    return (size_t)sh.NS * sh.stage_bytes + (size_t)(K / kUnitK) * 12 * sizeof(uint2);
+    // at least 80 KB, so that no more than two CTAs share an SM's tensor memory
+    const size_t need = (size_t)sh.NS * kStageBytes + 2 * (size_t)mma_xstride(K);
+    return need > 80 * 1024 ? need : 80 * 1024;
 }
 
-// Ring of about ring_bytes (2..16 stages); grid so that every CTA owns at least
-// one group's worth of units (a group is then cut between at most two CTAs).
+// Ring of about ring_bytes (2..16 stages); one CTA per SM (at most U).
 inline bool mma_plan(uint32_t Mp, uint32_t K, uint32_t nsm, uint32_t ring_bytes, MmaShape& sh, uint32_t& grid) {
-    if (K % kUnitK || Mp % kUnitRows || Mp == 0) return false;
-    sh.stage_bytes = kMmaStageUnits * kUnitBytes;
-    uint32_t ns = ring_bytes / sh.stage_bytes;
+    if (K % kTileK || Mp % kTileRows || Mp == 0 || K == 0) return false;
+    uint32_t ns = ring_bytes / kStageBytes;
     if (ns < 2) ns = 2;
     if (ns > kMmaMaxRing) ns = kMmaMaxRing;
     sh.NS = ns;
-    const uint32_t groups = Mp / kUnitRows;
-    grid = nsm < groups ? nsm : groups;
-    return mma_smem(sh, K) <= 220 * 1024;
+    sh.xstride = mma_xstride(K);
+    uint32_t cols = 32;
+    while (cols < ns * kStageTiles * kTileCols) cols <<= 1;
+    sh.tmem_cols = cols;
+    const uint64_t U = (uint64_t)(Mp / kTileRows) * (K / kTileK);
+    grid = (uint32_t)(U < nsm ? U : nsm);
+    return mma_smem(sh, K) <= 220 * 1024 && (cols <= 256 || mma_smem(sh, K) > 114 * 1024);
 }
 
 // Default ring: what leaves two CTAs per SM co-resident (228 KB of shared
-// memory per SM, 1 KB reserved per CTA, ~4.7 KB static), so that under
+// memory per SM, 1 KB reserved per CTA, ~6 KB static), so that under
 // programmatic dependent launch the next GEMV's CTAs start streaming their
 // weights while this one drains.
-constexpr uint32_t kMmaCoResidentDyn = 108 * 1024;
+constexpr uint32_t kMmaCoResidentDyn = 106 * 1024;
 
 inline uint32_t mma_ring_bytes(uint32_t K) {
     static int env_kb = -1;
@@ -574,14 +643,17 @@ inline uint32_t mma_ring_bytes(uint32_t K) {
         env_kb = v ? std::atoi(v) : 0;
     }
     if (env_kb >= 36 && env_kb <= 200) return (uint32_t)env_kb * 1024;
-    const uint32_t digits = (K / kUnitK) * 96, two = 2 * kMmaStageUnits * kUnitBytes;
+    const uint32_t digits = 2 * mma_xstride(K), two = 2 * kStageBytes;
     return kMmaCoResidentDyn > digits + two ? kMmaCoResidentDyn - digits : two;
 }
 
-inline uint32_t mma_grid(uint32_t Mp, uint32_t nsm) {
-    const uint32_t groups = Mp / kUnitRows;
-    return nsm < groups ? nsm : groups;
+inline uint32_t mma_grid(uint32_t Mp, uint32_t K, uint32_t nsm) {
+    const uint64_t U = (uint64_t)(Mp / kTileRows) * (K / kTileK);
+    return (uint32_t)(U < nsm ? U : nsm);
 }
+
+// Row tiles of an Mp-row matrix: the split scratch needs one ticket per row tile.
+inline uint32_t mma_row_tiles(uint32_t Mp) { return Mp / kTileRows; }
 
 template <class Pro, class Epi>
 cudaError_t launch_gemv_mma(const UnitW& W, const Pro& pro, const Epi& epi, SplitScratch sp, uint32_t* err,

@@ -23,7 +23,7 @@ cudaError_t launch_repack_q8_0(const void* blocks, int8_t* qs, float* scales, ui
 // 36-byte blocks -> 576-byte mma units (rows padded to 16; the caller zeroes padding).
 cudaError_t launch_pack_units(const void* blocks, uint8_t* units, uint32_t M, uint32_t K, RowMap map,
                               cudaStream_t s);
-inline uint64_t unit_bytes(uint32_t M, uint32_t K) { return (uint64_t)((M + 15) / 16) * (K / 32) * 576; }
+inline uint64_t unit_bytes(uint32_t M, uint32_t K) { return (uint64_t)((M + 127) / 128) * (K / 32) * 4608; }
 cudaError_t launch_gen_normal(uint64_t seed, uint64_t stream_id, uint64_t offset, uint64_t n, float k,
                               float* out, cudaStream_t s);
 cudaError_t launch_fill(float* out, uint64_t n, float v, cudaStream_t s);

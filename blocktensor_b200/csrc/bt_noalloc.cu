@@ -1,7 +1,7 @@
-// bt_noalloc.cu -- the unit-layout GEMV for callers that cannot allocate.
+// bt_noalloc.cu -- the tile-layout GEMV for callers that cannot allocate.
 //
-// bt_cuda_gemv_q8_units takes the scratch it needs for row groups split
-// between two CTAs (partial sums, arrival tickets, a timeout flag) from a
+// bt_cuda_gemv_q8_units takes the scratch it needs for row tiles split
+// between CTAs (partial sums, arrival tickets, a timeout flag) from a
 // per-device workspace that it cudaMallocs on first use.  Some callers cannot
 // allow that: an engine that reserves all device memory up front in its own
 // pool, a host runtime whose allocator must see every byte, or code that must
@@ -90,7 +90,7 @@ extern "C" int bt_cuda_gemv_q8_units_noalloc(const void* units, const float* x, 
     // tickets and the timeout flag start at zero on every call (an earlier call
     // that timed out may have left them set); the partial sums need no clearing
     BT_CUDA_CHECK(cudaMemsetAsync(ticket, 0, kNoAllocTicketBytes, s));
-    const UnitW w{static_cast<const uint8_t*>(units), M, (M + 15) / 16 * 16, K};
+    const UnitW w{static_cast<const uint8_t*>(units), M, unit_rows(M), K};
     BT_CUDA_CHECK(launch_gemv_mma(w, MProCopy{x}, SEpiStore{y}, SplitScratch{part, ticket}, err, d->nsm, s, false));
     return BT_OK;
 }

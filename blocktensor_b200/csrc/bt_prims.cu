@@ -16,9 +16,11 @@ namespace bt {
 // Per-device workspace of the standalone tensor-core GEMV: partial sums of
 // row groups cut between two CTAs ([num_sms][32] floats), their tickets
 // ([num_sms], zero between launches) and the bounded-wait error flag.
+constexpr uint32_t kWsTickets = 8192;  // row tiles: M <= 1048576
+
 struct GemvWorkspace {
-    float* part = nullptr;
-    uint32_t* ticket = nullptr;  // num_sms tickets followed by the error flag
+    float* part = nullptr;       // [num_sms][2][128] partial sums of split row tiles
+    uint32_t* ticket = nullptr;  // kWsTickets tickets followed by the error flag
     uint32_t nsm = 0;
 };
 
@@ -34,9 +36,9 @@ static int gemv_workspace(int dev, GemvWorkspace** out) {
         BT_CUDA_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
         float* part = nullptr;
         uint32_t* ticket = nullptr;
-        BT_CUDA_CHECK(cudaMalloc(&part, sizeof(float) * 32 * nsm));
-        cudaError_t e = cudaMalloc(&ticket, sizeof(uint32_t) * (nsm + 1));
-        if (e == cudaSuccess) e = cudaMemset(ticket, 0, sizeof(uint32_t) * (nsm + 1));
+        BT_CUDA_CHECK(cudaMalloc(&part, sizeof(float) * 2 * kTileRows * nsm));
+        cudaError_t e = cudaMalloc(&ticket, sizeof(uint32_t) * (kWsTickets + 1));
+        if (e == cudaSuccess) e = cudaMemset(ticket, 0, sizeof(uint32_t) * (kWsTickets + 1));
         if (e != cudaSuccess) {
             cudaFree(part);
             if (ticket) cudaFree(ticket);
@@ -365,15 +367,16 @@ int bt_cuda_gemv_q8_units(const void* units, const float* x, float* y, uint32_t 
     BT_CHECK_ARG(units && x && y, "gemv_q8_units: null buffer");
     BT_CHECK_ARG(((uintptr_t)units & 15) == 0 && ((uintptr_t)x & 15) == 0,
                  "gemv_q8_units: units and x must be 16-byte aligned");
+    BT_CHECK_ARG(M <= kWsTickets * kTileRows, "gemv_q8_units: M above 1048576 rows not supported");
     if (M == 0) return BT_OK;
     int dev = 0;
     BT_CUDA_CHECK(cudaGetDevice(&dev));
     GemvWorkspace* ws = nullptr;
     int rc = gemv_workspace(dev, &ws);
     if (rc != BT_OK) return rc;
-    const UnitW w{static_cast<const uint8_t*>(units), M, (M + 15) / 16 * 16, K};
+    const UnitW w{static_cast<const uint8_t*>(units), M, unit_rows(M), K};
     BT_CUDA_CHECK(launch_gemv_mma(w, MProCopy{x}, SEpiStore{y}, SplitScratch{ws->part, ws->ticket},
-                                  ws->ticket + ws->nsm, ws->nsm, as_stream(stream), false));
+                                  ws->ticket + kWsTickets, ws->nsm, as_stream(stream), false));
     return BT_OK;
 }
 

@@ -1,6 +1,6 @@
 // bt_ptx.cuh -- thin wrappers over the PTX the kernels need: mbarriers,
-// 1-D bulk (TMA) copies, named barriers, %globaltimer and the s8 tensor-core
-// MMA.  No multicast form of any copy is used anywhere.
+// 1-D bulk (TMA) copies, named barriers, %globaltimer, and tcgen05 (tensor
+// memory, int8 MMA).  No multicast form of any copy is used anywhere.
 #pragma once
 
 #include "bt_common.cuh"
@@ -74,16 +74,67 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
-// Barrier among the first 256 threads of the CTA (named barrier 1).
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// Named barrier 1: the 320 threads of warps 1-10 of the GEMV (digit builders).
+__device__ __forceinline__ void digit_sync() { asm volatile("bar.sync 1, 320;" ::: "memory"); }
 
-// D = A(16x32 s8, row) * B(32x8 s8, col) + 0, 32-bit integer accumulation.
-__device__ __forceinline__ void mma_s8_16832(const uint4& a, const uint2& b, int& d0, int& d1, int& d2, int& d3) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
-        : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
-        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(0));
+// Named barrier 2: warps 1-9 of the GEMV (tensor memory owner and its readers).
+__device__ __forceinline__ void tmem_sync() { asm volatile("bar.sync 2, 288;" ::: "memory"); }
+
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy reads (tensor cores, bulk copies) of the same bytes.
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ---------------------------------------------------------------- tcgen05
+
+__device__ __forceinline__ void tcgen05_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tcgen05_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Whole warp: allocates ncols (power of two, 32..512) tensor-memory columns;
+// the base address is written to *dst.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+                 : "memory");
 }
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Shared-memory matrix descriptor, no swizzle: start address, leading (K
+// direction) and stride (M/N direction) byte offsets between core matrices,
+// descriptor version 1.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, int8 x int8 -> int32 (one thread issues).
+__device__ __forceinline__ void umma_s8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// The mbarrier receives one arrival when all earlier MMAs of this thread are complete.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Warp: 16 consecutive 32-bit columns of the 32 tensor-memory lanes of this warp's quarter.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&d)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]), "=r"(d[4]), "=r"(d[5]), "=r"(d[6]), "=r"(d[7]), "=r"(d[8]),
+          "=r"(d[9]), "=r"(d[10]), "=r"(d[11]), "=r"(d[12]), "=r"(d[13]), "=r"(d[14]), "=r"(d[15])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Exact int -> float for |v| < 2^22 with two full-rate ops.
 __device__ __forceinline__ float small_i2f(int v) {

@@ -93,12 +93,12 @@ __global__ void repack_q8_0_kernel(const uint8_t* __restrict__ blocks, int8_t* _
     out[1] = make_int4((int)w[5], (int)w[6], (int)w[7], (int)w[8]);
 }
 
-// One thread per (row, 32-block) of a 36-byte-block matrix -> the 576-byte unit
-// layout of the tensor-core GEMV: destination row dr lands in group dr/16, row
-// rl = dr%16 of the unit; its 32 int8 go to the mma A-fragment slots (lane
-// (rl%8)*4 + tig, register 2*kh + rl/8 holds columns 16*kh + 4*tig .. +3) and
-// its scale to float 2*(rl%8) + rl/8 after the 512 weight bytes (rows r and
-// r+8 adjacent).  Padding rows stay zero.
+// One thread per (row, 32-block) of a 36-byte-block matrix -> the 4608-byte
+// tile layout of the tensor-core GEMV: destination row dr lands in row tile
+// dr/128, row rl = dr%128 of tile (dr/128, b); its 32 int8 go to the UMMA
+// K-major canonical layout (bytes 0-15 to offset (rl/8)*256 + (rl%8)*16, bytes
+// 16-31 to that + 128) and its scale to float rl after the 4096 weight bytes.
+// Padding rows stay zero.
 __global__ void pack_units_kernel(const uint8_t* __restrict__ blocks, uint8_t* __restrict__ units, uint32_t M,
                                   uint32_t K, RowMap map) {
     const uint64_t nb = (uint64_t)M * (K / 32);
@@ -108,14 +108,12 @@ __global__ void pack_units_kernel(const uint8_t* __restrict__ blocks, uint8_t* _
     const uint32_t r = (uint32_t)(i / bpr), b = (uint32_t)(i % bpr);
     const uint32_t* w = reinterpret_cast<const uint32_t*>(blocks + i * 36);
     const uint32_t dr = map_row(r, map);
-    const uint32_t rl = dr % 16, grp = rl % 8, upper = rl / 8;
-    uint8_t* unit = units + ((uint64_t)(dr / 16) * bpr + b) * 576;
-    reinterpret_cast<uint32_t*>(unit + 512)[grp * 2 + upper] = w[0];  // scales as (r, r + 8) pairs
-#pragma unroll
-    for (uint32_t kh = 0; kh < 2; ++kh)
-#pragma unroll
-        for (uint32_t tig = 0; tig < 4; ++tig)
-            *reinterpret_cast<uint32_t*>(unit + (grp * 4 + tig) * 16 + (kh * 2 + upper) * 4) = w[1 + kh * 4 + tig];
+    const uint32_t rl = dr % 128;
+    uint8_t* tile = units + ((uint64_t)(dr / 128) * bpr + b) * 4608;
+    reinterpret_cast<uint32_t*>(tile + 4096)[rl] = w[0];
+    uint8_t* q = tile + (rl / 8) * 256 + (rl % 8) * 16;
+    *reinterpret_cast<uint4*>(q) = make_uint4(w[1], w[2], w[3], w[4]);
+    *reinterpret_cast<uint4*>(q + 128) = make_uint4(w[5], w[6], w[7], w[8]);
 }
 
 __device__ __forceinline__ uint64_t splitmix64(uint64_t z) {

@@ -135,20 +135,20 @@ BT_API int bt_cuda_matvec_q8_0(const void* W_blocks, const float* X, float* Y,
 BT_API int bt_cuda_repack_q8_0(const void* W_blocks, int8_t* qs, float* scales,
                         uint32_t M, uint32_t K, void* stream);
 
-/* Repack reference blocks into the tensor-core unit layout used by the decode
- * engine: rows in groups of 16, each group as K/32 units of 576 bytes (the
- * 16x32 int8 block in mma fragment order, then its 16 fp32 scales in row
- * order 0, 8, 1, 9, ..., 7, 15).  `units`
- * must hold ceil(M/16) * (K/32) * 576 bytes; padding rows are zeroed.  Upload
+/* Repack reference blocks into the tensor-core tile layout used by the decode
+ * engine: rows in tiles of 128, each row tile as K/32 tiles of 4608 bytes (the
+ * 128x32 int8 block in the UMMA K-major no-swizzle canonical layout, then its
+ * 128 fp32 scales in row order).  `units` must be 16-byte aligned and hold
+ * ceil(M/128) * (K/32) * 4608 bytes; padding rows are zeroed.  Upload
  * repack of MemoryManager::copy_host_to_device (memory/memory_manager.cpp:22-42). */
 BT_API int bt_cuda_pack_q8_units(const void* W_blocks, void* units, uint32_t M, uint32_t K, void* stream);
 
-/* y[m] = sum_k W[m][k] x[k] on the unit layout: quantization::matvec_q8_0
- * (quant_types.cpp:101-121) on the tensor cores (exact int8 block dot products,
- * x as 22-bit fixed point, fp32 block accumulation), split evenly over all SMs.
- * units and x must be 16-byte aligned.  Scratch for row groups split between
- * two CTAs comes from a per-device workspace the library allocates on the
- * first call. */
+/* y[m] = sum_k W[m][k] x[k] on the tile layout: quantization::matvec_q8_0
+ * (quant_types.cpp:101-121) on the tensor cores (tcgen05 int8 MMA: exact block
+ * dot products, x as 22-bit fixed point, fp32 block accumulation), split evenly
+ * over all SMs.  units and x must be 16-byte aligned; M <= 1048576.  Scratch for
+ * row tiles split between CTAs comes from a per-device workspace the library
+ * allocates on the first call. */
 BT_API int bt_cuda_gemv_q8_units(const void* units, const float* x, float* y, uint32_t M, uint32_t K,
                                  void* stream);
 
