@@ -24,17 +24,18 @@
 // CTAs is finished by the one that completes last, adding the CTAs' partial
 // sums in CTA order, so results are deterministic.
 //
-// Warp roles (352 threads): warp 0 produces (cp.async.bulk of 4-tile stages
+// Warp roles (320 threads): warp 0 produces (cp.async.bulk of 4-tile stages
 // into an mbarrier ring; weights never depend on the previous kernel, so under
 // programmatic dependent launch the ring fills while the previous kernel
-// drains); warp 1 owns the tensor memory and one of its lanes issues the MMAs;
-// warps 2-9 read the digit sums from tensor memory (warp w reads TMEM lanes
-// 32 (w%4) .. +31, the two warps of a lane quarter take alternate tile pairs)
-// and accumulate; warp 10 finishes each row tile (cross-CTA merge, epilogue).
-// Warps 1-10 build the digits first.  No thread loads weights into registers:
-// the tensor cores read them from the ring, which leaves the SM's shared
-// memory path to the bulk copies.  All waits are bounded (2 s); an expired wait
-// sets *err and the CTA still finishes and frees its tensor memory.
+// drains); warps 1-4 issue the MMAs, warp 1+t for tile t of every stage (one
+// thread issuing a tcgen05.mma spends ~130 cycles on it, so a single issuer
+// could not keep up with HBM); warps 5-8 read the digit sums from tensor
+// memory (warp w reads TMEM lanes 32 (w%4) .. +31, all four tiles of a stage
+// with one load) and accumulate; warp 9 finishes each row tile (cross-CTA
+// merge, epilogue).  Warps 1-9 build the digits first.  Warp 1 owns the tensor
+// memory.  No thread loads weights into registers: the tensor cores read them
+// from the ring.  All waits are bounded (2 s); an expired wait sets *err and
+// the CTA still finishes and frees its tensor memory.
 #pragma once
 
 #include "bt_common.cuh"
@@ -50,13 +51,14 @@ constexpr uint32_t kTileBytes = 4608;    // + 128 fp32 scales
 constexpr uint32_t kStageTiles = 4;      // 18 KB stages
 constexpr uint32_t kStageBytes = kStageTiles * kTileBytes;
 constexpr uint32_t kTileCols = 8;        // TMEM columns per tile (N = 8)
-constexpr int kMmaThreads = 352;
+constexpr int kMmaThreads = 320;
 constexpr int kProducerWarp = 0;
-constexpr int kMmaWarp = 1;
-constexpr int kAccWarp0 = 2;             // accumulator warps 2..9
-constexpr int kAccWarps = 8;
-constexpr int kFinWarp = 10;
-constexpr int kDigitThreads = 320;       // warps 1..10
+constexpr int kMmaWarp0 = 1;             // MMA issuers 1..4 (warp 1 owns the tensor memory)
+constexpr int kAccWarp0 = 5;             // accumulator warps 5..8
+constexpr int kAccWarps = 4;
+constexpr int kFinWarp = 9;
+constexpr int kDigitWarps = 9;           // warps 1..9
+constexpr int kDigitThreads = 32 * kDigitWarps;
 constexpr int kRedSlots = 4;
 constexpr uint32_t kMmaMaxRing = 16;     // stages (16 x 32 TMEM columns = 512)
 
@@ -170,13 +172,13 @@ __device__ __forceinline__ void pack_item(uint8_t* xb, uint32_t xstride, uint32_
 
 // Builds the digit arrays and returns the exponent e; *bad when the vector
 // holds an inf or NaN (the outputs are then NaN).  One global round trip: item
-// idx is loaded once into registers by digit thread idx % 320 (K <= 12800;
-// larger vectors load their tail twice).  Called by the 320 threads of warps
-// 1-10 (tid = 0..319); ends with the digits visible to the tensor cores.
+// idx is loaded once into registers by digit thread idx % 288 (K <= 13824;
+// larger vectors load their tail twice).  Called by the 288 threads of warps
+// 1-9 (tid = 0..287); ends with the digits visible to the tensor cores.
 template <class Pro>
 __device__ int build_digits(const Pro& pro, uint32_t K, uint8_t* xb, uint32_t xstride, float* red, uint32_t tid,
                             bool& bad) {
-    constexpr int R = 5;
+    constexpr int R = 6;
     const float* s = pro.base(K);
     const uint32_t items = K >> 3;
     float ss = 0.0f, mx = 0.0f;
@@ -195,15 +197,15 @@ __device__ int build_digits(const Pro& pro, uint32_t K, uint8_t* xb, uint32_t xs
         pro.load(s, k, ss, mx);
         pro.load(s, k + 16, ss, mx);
     }
-    // sum and max over the 10 warps
+    // sum and max over the digit warps
     ss = warp_sum(ss);
     mx = warp_max(mx);
     const uint32_t lane = tid & 31, w = tid >> 5;
-    if (lane == 0) { red[w] = ss; red[10 + w] = mx; }
+    if (lane == 0) { red[w] = ss; red[kDigitWarps + w] = mx; }
     digit_sync();
     float tss = 0.0f, tmx = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 10; ++i) { tss += red[i]; tmx = fmaxf(tmx, red[10 + i]); }
+    for (int i = 0; i < kDigitWarps; ++i) { tss += red[i]; tmx = fmaxf(tmx, red[kDigitWarps + i]); }
     const float f = pro.factor(tss, K);
     const float m = tmx * f;
     // m * 2^e in [2^20, 2^21): values round to |v| <= 2^21 (slack for the rounding of m)
@@ -394,9 +396,9 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[kMmaMaxRing], empty[kMmaMaxRing], mma_done[kMmaMaxRing];
     __shared__ __align__(8) uint64_t red_full[kRedSlots], red_free[kRedSlots];
-    __shared__ float red[kRedSlots][2][kTileRows];
+    __shared__ float red[kRedSlots][kTileRows];
     __shared__ float fin[kTileRows];
-    __shared__ float red20[20];
+    __shared__ float redd[2 * kDigitWarps];
     __shared__ uint32_t s_tmem;
 
     pdl_trigger();
@@ -416,7 +418,7 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
         for (uint32_t s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kAccWarps);
-            mbar_init(&mma_done[s], 1);
+            mbar_init(&mma_done[s], kStageTiles);  // one commit per issuer
         }
         for (int r = 0; r < kRedSlots; ++r) {
             mbar_init(&red_full[r], kAccWarps);
@@ -424,7 +426,7 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
         }
         fence_mbar_init();
     }
-    if (warp == kMmaWarp) {
+    if (warp == kMmaWarp0) {
         tmem_alloc(&s_tmem, sh.tmem_cols);
         tmem_relinquish();
     }
@@ -465,43 +467,43 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
         return;
     }
 
-    // ---------------- warps 1-10: the input vector's digits (every thread gets e and bad)
+    // ---------------- warps 1-9: the input vector's digits (every thread gets e and bad)
     pdl_wait();
     bool bad = false;
-    const int e = build_digits(pro, K, xb, sh.xstride, red20, threadIdx.x - 32, bad);
+    const int e = build_digits(pro, K, xb, sh.xstride, redd, threadIdx.x - 32, bad);
 
-    if (warp == kMmaWarp) {
-        // ---------------- MMA issue (one lane), then tensor memory release
+    if (warp < kAccWarp0) {
+        // ---------------- MMA issue: lane 0 of warp 1+t issues tile t of every stage
+        const uint32_t t = warp - kMmaWarp0;
         if (lane == 0) {
             bool ok = true;
-            uint32_t s = 0, ph = 0, b = u0 % NB;
-            const uint32_t xaddr = smem_u32(xb);
+            uint32_t s = 0, ph = 0, b = (u0 + t) % NB;
+            // descriptors advance by adding to the start-address field (addresses < 256 KB: no carry)
+            const uint64_t a0 = umma_desc(smem_u32(ring + t * kTileBytes), 128, 256);
+            const uint64_t b0 = umma_desc(smem_u32(xb), sh.xstride, 128);
+            const uint32_t d0 = tmem + t * kTileCols;
             for (uint32_t j = 0; j < nstages; ++j) {
                 if (ok) ok = mbar_wait(&full[s], ph, err);
                 tcgen05_fence_after();
-                const uint32_t n = min(kStageTiles, u1 - (u0 + j * kStageTiles));
-                const uint32_t abase = smem_u32(ring + (size_t)s * kStageBytes);
-                for (uint32_t t = 0; t < n; ++t) {
-                    if (ok) {
-                        const uint64_t ad = umma_desc(abase + t * kTileBytes, 128, 256);
-                        const uint64_t bd = umma_desc(xaddr + b * 48, sh.xstride, 128);
-                        umma_s8(tmem + s * (kStageTiles * kTileCols) + t * kTileCols, ad, bd, kIdescS8, 0);
-                    }
-                    if (++b == NB) b = 0;
-                }
-                umma_commit(&mma_done[s]);  // arrives once the stage's MMAs are complete
+                if (ok && t < min(kStageTiles, u1 - (u0 + j * kStageTiles)))
+                    umma_s8(d0 + s * (kStageTiles * kTileCols), a0 + ((s * kStageBytes) >> 4), b0 + b * 3, kIdescS8, 0);
+                umma_commit(&mma_done[s]);  // arrives once this issuer's MMAs are complete
                 if (++s == NS) { s = 0; ph ^= 1; }
+                b += kStageTiles;
+                while (b >= NB) b -= NB;
             }
         }
         __syncwarp();
         tmem_sync();  // every accumulator warp is done with tensor memory
-        tcgen05_fence_after();
-        tmem_dealloc(tmem, sh.tmem_cols);
+        if (warp == kMmaWarp0) {
+            tcgen05_fence_after();
+            tmem_dealloc(tmem, sh.tmem_cols);
+        }
         return;
     }
 
     if (warp == kFinWarp) {
-        // ---------------- finisher: sum the two halves, cross-CTA merge, epilogue
+        // ---------------- finisher: 2^-e, cross-CTA merge, epilogue
         StreamState est{-INFINITY, 0xFFFFFFFFu};
         bool ok = true;
         uint32_t slot = 0, ph = 0;
@@ -509,10 +511,8 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
             if (ok) ok = mbar_wait(&red_full[slot], ph, err);
             float v[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int r = lane + 32 * i;
-                v[i] = bad ? __int_as_float(0x7fc00000) : ldexpf(red[slot][0][r] + red[slot][1][r], -e);
-            }
+            for (int i = 0; i < 4; ++i)
+                v[i] = bad ? __int_as_float(0x7fc00000) : ldexpf(red[slot][lane + 32 * i], -e);
             __syncwarp();
             if (lane == 0) mbar_arrive(&red_free[slot]);
             if (++slot == kRedSlots) { slot = 0; ph ^= 1; }
@@ -551,16 +551,16 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
         return;
     }
 
-    // ---------------- accumulators: warp (quarter q, parity p) takes tiles 2p, 2p+1 of every stage
-    const uint32_t q = warp & 3, p = (warp - kAccWarp0) >> 2;
+    // ---------------- accumulators: warp 5+i reads TMEM lane quarter (5+i)%4, all tiles of every stage
+    const uint32_t q = warp & 3;
     const uint32_t row = 32 * q + lane;
-    const uint32_t taddr = tmem + ((32 * q) << 16) + 16 * p;
+    const uint32_t taddr = tmem + ((32 * q) << 16);
     float acc = 0.0f;
     bool ok = true;
     uint32_t cur_g = g_first, rslot = 0, rph = 0, gi = 0;
     auto flush = [&]() {
         if (gi >= kRedSlots && ok) ok = mbar_wait(&red_free[rslot], rph ^ 1, err);
-        red[rslot][p][row] = acc;
+        red[rslot][row] = acc;
         __syncwarp();
         if (lane == 0) mbar_arrive(&red_full[rslot]);
         acc = 0.0f;
@@ -568,36 +568,35 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
         if (++rslot == kRedSlots) { rslot = 0; rph ^= 1; }
         ++cur_g;
     };
-    uint32_t g = (u0 + 2 * p) / NB;             // row tile and block of the warp's first tile
-    uint32_t b = (u0 + 2 * p) - g * NB;
+    uint32_t g = u0 / NB, b = u0 - g * NB;  // row tile and block of the next tile
     uint32_t s = 0, ph = 0;
     for (uint32_t j = 0; j < nstages; ++j) {
         if (ok) ok = mbar_wait(&mma_done[s], ph, err);
         tcgen05_fence_after();
-        uint32_t d[16];
-        tmem_ld16(taddr + s * (kStageTiles * kTileCols), d);
+        uint32_t d[32];
+        tmem_ld32(taddr + s * (kStageTiles * kTileCols), d);
         const uint32_t n = min(kStageTiles, u1 - (u0 + j * kStageTiles));
         const uint8_t* st = ring + (size_t)s * kStageBytes + kTileQBytes + row * 4;
-        const float sc0 = 2 * p < n ? *reinterpret_cast<const float*>(st + (2 * p) * kTileBytes) : 0.0f;
-        const float sc1 = 2 * p + 1 < n ? *reinterpret_cast<const float*>(st + (2 * p + 1) * kTileBytes) : 0.0f;
+        float sc[kStageTiles];
+#pragma unroll
+        for (uint32_t t = 0; t < kStageTiles; ++t)
+            sc[t] = t < n ? *reinterpret_cast<const float*>(st + t * kTileBytes) : 0.0f;
         tmem_wait_ld();
         tcgen05_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);  // stage (smem and TMEM columns) free
         if (++s == NS) { s = 0; ph ^= 1; }
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-            if (2 * p + t < n) {
+        for (uint32_t t = 0; t < kStageTiles; ++t) {
+            if (t < n) {
                 while (cur_g < g) flush();
-                const uint32_t* dt = d + 8 * t;  // columns hi, mid, lo of this tile
+                const uint32_t* dt = d + kTileCols * t;  // columns hi, mid, lo of tile t
                 const float y = fmaf(fmaf(small_i2f((int)dt[0]), 256.0f, small_i2f((int)dt[1])), 256.0f,
                                      small_i2f((int)dt[2]));
-                acc = fmaf(t ? sc1 : sc0, y, acc);
+                acc = fmaf(sc[t], y, acc);
             }
             if (++b == NB) { b = 0; ++g; }
         }
-        b += kStageTiles - 2;  // the other parity's tiles of the stage
-        while (b >= NB) { b -= NB; ++g; }
     }
     while (cur_g <= g_last) flush();
     tcgen05_fence_before();
@@ -630,11 +629,11 @@ inline bool mma_plan(uint32_t Mp, uint32_t K, uint32_t nsm, uint32_t ring_bytes,
     return mma_smem(sh, K) <= 220 * 1024 && (cols <= 256 || mma_smem(sh, K) > 114 * 1024);
 }
 
-// Default ring: what leaves two CTAs per SM co-resident (228 KB of shared
-// memory per SM, 1 KB reserved per CTA, ~6 KB static), so that under
-// programmatic dependent launch the next GEMV's CTAs start streaming their
-// weights while this one drains.
-constexpr uint32_t kMmaCoResidentDyn = 106 * 1024;
+// Default ring: about 150 KB of shared memory per CTA (one CTA per SM).
+// Measured on the 7B decode step, a deep ring beats two co-resident CTAs with
+// half the ring each (the next GEMV then streams under programmatic dependent
+// launch, but every GEMV has half the bytes in flight).
+constexpr uint32_t kMmaCoResidentDyn = 150 * 1024;
 
 inline uint32_t mma_ring_bytes(uint32_t K) {
     static int env_kb = -1;

@@ -74,11 +74,11 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
-// Named barrier 1: the 320 threads of warps 1-10 of the GEMV (digit builders).
-__device__ __forceinline__ void digit_sync() { asm volatile("bar.sync 1, 320;" ::: "memory"); }
+// Named barrier 1: the 288 threads of warps 1-9 of the GEMV (digit builders).
+__device__ __forceinline__ void digit_sync() { asm volatile("bar.sync 1, 288;" ::: "memory"); }
 
-// Named barrier 2: warps 1-9 of the GEMV (tensor memory owner and its readers).
-__device__ __forceinline__ void tmem_sync() { asm volatile("bar.sync 2, 288;" ::: "memory"); }
+// Named barrier 2: warps 1-8 of the GEMV (MMA issuers and tensor-memory readers).
+__device__ __forceinline__ void tmem_sync() { asm volatile("bar.sync 2, 256;" ::: "memory"); }
 
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy reads (tensor cores, bulk copies) of the same bytes.
@@ -131,6 +131,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&d)[16]) {
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]), "=r"(d[4]), "=r"(d[5]), "=r"(d[6]), "=r"(d[7]), "=r"(d[8]),
           "=r"(d[9]), "=r"(d[10]), "=r"(d[11]), "=r"(d[12]), "=r"(d[13]), "=r"(d[14]), "=r"(d[15])
+        : "r"(taddr)
+        : "memory");
+}
+// Warp: 32 consecutive 32-bit columns of the 32 tensor-memory lanes of this warp's quarter.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&d)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]), "=r"(d[4]), "=r"(d[5]), "=r"(d[6]), "=r"(d[7]), "=r"(d[8]),
+          "=r"(d[9]), "=r"(d[10]), "=r"(d[11]), "=r"(d[12]), "=r"(d[13]), "=r"(d[14]), "=r"(d[15]), "=r"(d[16]),
+          "=r"(d[17]), "=r"(d[18]), "=r"(d[19]), "=r"(d[20]), "=r"(d[21]), "=r"(d[22]), "=r"(d[23]), "=r"(d[24]),
+          "=r"(d[25]), "=r"(d[26]), "=r"(d[27]), "=r"(d[28]), "=r"(d[29]), "=r"(d[30]), "=r"(d[31])
         : "r"(taddr)
         : "memory");
 }
