@@ -17,7 +17,7 @@ CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libbt_cuda.so")
 
 SOURCES = ["bt_quant.cu", "bt_prims.cu", "bt_engine.cu", "bt_noalloc.cu"]
-HEADERS = ["bt_common.cuh", "bt_gemv.cuh", "bt_gemv_mma.cuh", "bt_ptx.cuh", "bt_attention.cuh", "bt_internal.h"]
+HEADERS = ["bt_common.cuh", "bt_gemv.cuh", "bt_gemv_mma.cuh", "bt_ptx.cuh", "bt_attention.cuh", "bt_step.cuh", "bt_internal.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr",

@@ -182,4 +182,10 @@ template <> struct KVConv<__half> {
     __device__ static __half from_f(float v) { return __float2half_rn(v); }
 };
 
+// Cache element loaded through L2 (rows may have been written by another SM in the same kernel).
+__device__ __forceinline__ float ldcg_kv(const float* p) { return __ldcg(p); }
+__device__ __forceinline__ __half ldcg_kv(const __half* p) {
+    return __ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(p)));
+}
+
 }  // namespace bt

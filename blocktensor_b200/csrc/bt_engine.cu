@@ -18,6 +18,7 @@
 #include "bt_gemv.cuh"
 #include "bt_gemv_mma.cuh"
 #include "bt_attention.cuh"
+#include "bt_step.cuh"
 #include "bt_internal.h"
 
 #include <cmath>
@@ -49,6 +50,12 @@ struct bt_engine {
     bool pdl = true;
     bool use_graph = true;
     uint32_t prefetch_bytes = 98304;  // L2 prefetch of the next GEMV's weights, per CTA
+    // persistent step kernel (one launch per token); the launch-per-kernel step stays for profiling
+    bool use_step = true;
+    bool step_ok = false;
+    uint32_t step_nv = 0, step_ns = 0, step_xstride = 0, step_tmem = 0, step_scratch_off = 0;
+    size_t step_smem = 0;
+    StepLayer* d_layers = nullptr;  // device copy of the per-layer matrix table
     uint32_t num_sms = 148;
     bool taps_on = false;
     std::vector<void*> allocs;
@@ -91,6 +98,11 @@ struct bt_kv {
     uint64_t host_pos = 0;      // position of the next step, mirrored on the host for bounds checks
     cudaGraphExec_t graph = nullptr;
     bool graph_taps = false;
+    // persistent step kernel: phase counters [5 L + 1], attention split partials and tickets
+    uint32_t* step_cnt = nullptr;
+    float* step_att_part = nullptr;
+    uint32_t* step_att_ticket = nullptr;
+    uint32_t step_S = 1;
 };
 
 namespace {
@@ -181,6 +193,145 @@ int alloc_units(bt_engine* e, uint8_t** out, uint32_t M, uint32_t K, const char*
     return BT_OK;
 }
 
+// Shape of the persistent step kernel: head dims per lane, ring depth, shared
+// memory (ring + a scratch area for digits or attention partials).  Configs
+// whose query heads per KV head do not fit the kernel's registers use the
+// launch-per-kernel step.
+int plan_step(bt_engine* e) {
+    const auto& c = e->cfg;
+    const uint32_t hd = c.head_dim, GQ = c.num_heads / c.num_kv_heads;
+    e->step_nv = hd <= 64 ? 2 : hd <= 128 ? 4 : 8;
+    e->step_ok = GQ * e->step_nv <= 16 && hd % e->step_nv == 0;
+    const uint32_t kmax = c.dim > c.hidden_dim ? c.dim : c.hidden_dim;
+    size_t scratch = 2 * (size_t)mma_xstride(kmax);
+    const size_t attn = (size_t)kDigitWarps * GQ * (hd + 2) * 4;
+    if (attn > scratch) scratch = attn;
+    scratch = (scratch + 127) / 128 * 128;
+    const size_t budget = 220 * 1024;
+    if (scratch + 2 * kStageBytes > budget) e->step_ok = false;
+    uint32_t ns = scratch < budget ? (uint32_t)((budget - scratch) / kStageBytes) : 0;
+    if (ns > kMmaMaxRing) ns = kMmaMaxRing;
+    e->step_ns = ns;
+    e->step_xstride = mma_xstride(kmax);
+    e->step_scratch_off = ns * kStageBytes;
+    e->step_smem = (size_t)ns * kStageBytes + scratch;
+    uint32_t cols = 32;
+    while (cols < ns * kStageTiles * kTileCols) cols <<= 1;
+    e->step_tmem = cols;
+    if (const char* v = std::getenv("BT_STEP_KERNEL")) e->use_step = (v[0] != '0');
+    // the per-layer matrix table the kernel walks
+    std::vector<StepLayer> tab(c.num_layers);
+    const uint32_t D = c.dim, F = c.hidden_dim, QKV = D + 2 * kvd(c);
+    for (uint32_t l = 0; l < c.num_layers; ++l) {
+        const LayerDev& L = e->layers[l];
+        tab[l].qkv = StepMat{L.qkv, QKV, unit_rows(QKV), D};
+        tab[l].o = StepMat{L.o, D, unit_rows(D), D};
+        tab[l].gu = StepMat{L.gu, 2 * F, unit_rows(2 * F), D};
+        tab[l].d = StepMat{L.d, D, unit_rows(D), F};
+        tab[l].attn_norm = L.attn_norm;
+        tab[l].ffn_norm = L.ffn_norm;
+    }
+    BT_TRY_ALLOC(e->allocs, &e->d_layers, c.num_layers, "step layer table");
+    BT_CUDA_CHECK(cudaMemcpyAsync(e->d_layers, tab.data(), sizeof(StepLayer) * c.num_layers, cudaMemcpyHostToDevice,
+                                  e->stream));
+    BT_CUDA_CHECK(cudaStreamSynchronize(e->stream));
+    return BT_OK;
+}
+
+template <int NV, int GQM, typename KVT>
+cudaError_t launch_step_t(const StepArgs& a, uint32_t grid, size_t smem, cudaStream_t s) {
+    auto kern = decode_step_kernel<NV, GQM, KVT>;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!attr_set[dev]) {
+        cudaError_t ce = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        if (ce != cudaSuccess) return ce;
+        int blocks = 0;
+        ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, kMmaThreads, smem);
+        if (ce != cudaSuccess) return ce;
+        if (blocks < 1) return cudaErrorCooperativeLaunchTooLarge;
+        attr_set[dev] = true;
+    }
+    if (g_dry_run) return cudaSuccess;
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kMmaThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+// One decode step as one cooperative launch of the persistent kernel.
+int launch_step(bt_engine* e, bt_kv* kv, cudaStream_t s) {
+    const auto& c = e->cfg;
+    StepArgs a{};
+    a.layers = e->d_layers;
+    a.head = StepMat{e->head, c.vocab_size, unit_rows(c.vocab_size), c.dim};
+    a.embed = e->embed;
+    a.out_norm = e->out_norm;
+    a.x = e->x;
+    a.q = e->q;
+    a.attn = e->attn;
+    a.act = e->act;
+    a.logits = e->logits;
+    a.taps = e->taps_on ? e->taps : nullptr;
+    a.kc = kv->k;
+    a.vc = kv->v;
+    a.rope = kv->rope;
+    a.st = kv->st;
+    a.tok_hist = kv->tok_hist;
+    a.split_part = e->split_part;
+    a.split_ticket = e->split_ticket;
+    a.am_val = e->am_val;
+    a.am_idx = e->am_idx;
+    a.am_ticket = e->am_ticket;
+    a.att_part = kv->step_att_part;
+    a.att_ticket = kv->step_att_ticket;
+    a.cnt = kv->step_cnt;
+    a.L = c.num_layers;
+    a.D = c.dim;
+    a.KVD = kvd(c);
+    a.hd = c.head_dim;
+    a.KVH = c.num_kv_heads;
+    a.GQ = c.num_heads / c.num_kv_heads;
+    a.max_seq = kv->max_seq;
+    a.S_att = kv->step_S;
+    a.eps = c.rms_norm_eps;
+    a.scale = 1.0f / std::sqrt((float)c.head_dim);
+    a.NS = e->step_ns;
+    a.xstride = e->step_xstride;
+    a.tmem_cols = e->step_tmem;
+    a.scratch_off = e->step_scratch_off;
+    const uint32_t grid = e->num_sms;
+    cudaError_t ce;
+    const bool f16 = kv->dtype == BT_KV_FP16;
+    // query heads per KV head: 1 (multi-head) or up to 16 / NV (grouped-query)
+    const bool mha = a.GQ == 1;
+#define BT_STEP_LAUNCH(NV_)                                                                                      \
+    ce = mha ? (f16 ? launch_step_t<NV_, 1, __half>(a, grid, e->step_smem, s)                                   \
+                    : launch_step_t<NV_, 1, float>(a, grid, e->step_smem, s))                                   \
+             : (f16 ? launch_step_t<NV_, 16 / NV_, __half>(a, grid, e->step_smem, s)                            \
+                    : launch_step_t<NV_, 16 / NV_, float>(a, grid, e->step_smem, s))
+    switch (e->step_nv) {
+        case 2: BT_STEP_LAUNCH(2); break;
+        case 4: BT_STEP_LAUNCH(4); break;
+        default: BT_STEP_LAUNCH(8); break;
+    }
+#undef BT_STEP_LAUNCH
+    BT_CUDA_CHECK(ce);
+    return BT_OK;
+}
+
+bool step_path(const bt_engine* e) { return e->use_step && e->step_ok; }
+
 int alloc_weights(bt_engine* e) {
     const auto& c = e->cfg;
     const size_t D = c.dim, F = c.hidden_dim, KV = kvd(c), V = c.vocab_size;
@@ -218,7 +369,7 @@ int alloc_weights(bt_engine* e) {
     BT_TRY_ALLOC(A, &e->split_part, (size_t)e->num_sms * 2 * kTileRows, "split partials");
     BT_TRY_ALLOC(A, &e->split_ticket, tickets, "split tickets");
     BT_CUDA_CHECK(cudaMemsetAsync(e->split_ticket, 0, sizeof(uint32_t) * tickets, e->stream));
-    return BT_OK;
+    return plan_step(e);
 }
 
 void drop_graphs_of(bt_kv* kv) {
@@ -356,6 +507,14 @@ int ensure_graph(bt_engine* e, bt_kv* kv) {
 
 int run_steps(bt_engine* e, bt_kv* kv, uint32_t n, cudaStream_t s) {
     if (kv->host_pos + n > kv->max_seq) return fail(BT_ERR_OUT_OF_RANGE, "KVCache pos out of bounds");
+    if (step_path(e)) {
+        for (uint32_t i = 0; i < n; ++i) {
+            int rc = launch_step(e, kv, s);
+            if (rc != BT_OK) return rc;
+            kv->host_pos += 1;
+        }
+        return BT_OK;
+    }
     int rc = ensure_graph(e, kv);
     if (rc != BT_OK) return rc;
     for (uint32_t i = 0; i < n; ++i) {
@@ -595,7 +754,20 @@ int bt_kv_create(bt_engine* e, uint32_t max_seq, int dtype, bt_kv** out) {
         return cleanup(rc);
     if ((rc = dev_alloc(kv->allocs, &kv->att_ticket, (size_t)c.num_layers * c.num_kv_heads, "attention tickets")))
         return cleanup(rc);
+    // persistent step kernel: one attention item per (KV head, split), about one per SM
+    kv->step_S = e->num_sms / c.num_kv_heads;
+    if (kv->step_S < 1) kv->step_S = 1;
+    const uint32_t GQ = c.num_heads / c.num_kv_heads;
+    if ((rc = dev_alloc(kv->allocs, &kv->step_cnt, (size_t)5 * c.num_layers + 1, "phase counters")))
+        return cleanup(rc);
+    if ((rc = dev_alloc(kv->allocs, &kv->step_att_part,
+                        (size_t)c.num_kv_heads * GQ * kv->step_S * (c.head_dim + 2), "step attention partials")))
+        return cleanup(rc);
+    if ((rc = dev_alloc(kv->allocs, &kv->step_att_ticket, c.num_kv_heads, "step attention tickets")))
+        return cleanup(rc);
     cudaError_t ce = cudaMemsetAsync(kv->att_ticket, 0, sizeof(uint32_t) * c.num_layers * c.num_kv_heads, e->stream);
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(kv->step_cnt, 0, sizeof(uint32_t) * (5 * c.num_layers + 1), e->stream);
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(kv->step_att_ticket, 0, sizeof(uint32_t) * c.num_kv_heads, e->stream);
     if (ce == cudaSuccess) ce = cudaMemsetAsync(kb, 0, n * esz, e->stream);
     if (ce == cudaSuccess) ce = cudaMemsetAsync(vb, 0, n * esz, e->stream);
     if (ce == cudaSuccess) ce = cudaMemsetAsync(kv->st, 0, sizeof(DevState), e->stream);
@@ -679,6 +851,8 @@ int bt_engine_forward_token(bt_engine* e, bt_kv* kv, uint32_t token, uint32_t po
     h->cur_token = token;
     h->n_fixed = 0;
     BT_CUDA_CHECK(cudaMemcpyAsync(kv->st, h, sizeof(DevState), cudaMemcpyHostToDevice, s));
+    // the state's step count restarts at 0, and so do the phase counters
+    BT_CUDA_CHECK(cudaMemsetAsync(kv->step_cnt, 0, sizeof(uint32_t) * (5 * e->cfg.num_layers + 1), s));
     kv->host_pos = pos;
     rc = run_steps(e, kv, 1, s);
     if (rc != BT_OK) return rc;
@@ -708,9 +882,10 @@ int bt_engine_begin(bt_engine* e, bt_kv* kv, const uint32_t* prompt, uint32_t n_
     h->cur_token = prompt[0];
     h->n_fixed = pos0 + n_prompt;
     BT_CUDA_CHECK(cudaMemcpyAsync(kv->st, h, sizeof(DevState), cudaMemcpyHostToDevice, s));
+    BT_CUDA_CHECK(cudaMemsetAsync(kv->step_cnt, 0, sizeof(uint32_t) * (5 * e->cfg.num_layers + 1), s));
     BT_CUDA_CHECK(cudaStreamSynchronize(s));
     kv->host_pos = pos0;
-    return ensure_graph(e, kv);
+    return step_path(e) ? BT_OK : ensure_graph(e, kv);
 }
 
 int bt_engine_steps(bt_engine* e, bt_kv* kv, uint32_t n, void* stream) {
@@ -764,7 +939,7 @@ int bt_kv_step_info(bt_kv* kv, uint32_t context, uint64_t* launches, uint64_t* b
     const uint64_t emb = 4 * D;
     const uint64_t esz = kv->dtype == BT_KV_FP16 ? 2 : 4;
     const uint64_t kv_bytes = 2 * L * KV * esz * ((uint64_t)context + 1);  // read c positions, write 1
-    if (launches) *launches = 5 * L + 1;
+    if (launches) *launches = step_path(kv->e) ? 1 : 5 * L + 1;
     if (bytes) *bytes = weight_bytes + norms + emb + kv_bytes;
     return BT_OK;
 }

@@ -262,7 +262,7 @@ struct SEpiResidual {
         for (uint32_t t = lane; t < T; t += 32) {
             const uint32_t r = row0 + t;
             if (r >= M) continue;
-            const float v = __fadd_rn(x[r], rs(t));
+            const float v = __fadd_rn(__ldcg(x + r), rs(t));  // x may have been written by another SM
             x[r] = v;
             if (tap) tap[r] = v;
         }
@@ -369,6 +369,7 @@ struct SEpiLogits {
             st->last_argmax = ix;
             st->cur_token = next;
             st->pos = pos + 1;
+            if (e.bump_epoch) st->pad[0] += 1;
             *e.ticket = 0;
         }
     }
@@ -533,11 +534,23 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
                 __threadfence();
 #pragma unroll
                 for (int i = 0; i < 4; ++i) v[i] = 0.0f;
-                for (uint32_t cc = c_lo; cc <= c_hi; ++cc) {  // fixed order: CTA index
-                    const uint32_t first_cc = (uint32_t)(((uint64_t)U * cc) / G) / NB;
-                    const float* pc = sp.part + ((size_t)cc * 2 + (g == first_cc ? 0 : 1)) * kTileRows;
+                for (uint32_t cb = c_lo; cb <= c_hi; cb += 4) {  // 4 CTAs' partials in flight, summed in CTA order
+                    float pv[4][4];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) v[i] += __ldcg(pc + lane + 32 * i);
+                    for (uint32_t u = 0; u < 4; ++u) {
+                        const uint32_t cc = cb + u;
+                        if (cc > c_hi) break;
+                        const uint32_t first_cc = (uint32_t)(((uint64_t)U * cc) / G) / NB;
+                        const float* pc = sp.part + ((size_t)cc * 2 + (g == first_cc ? 0 : 1)) * kTileRows;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) pv[u][i] = __ldcg(pc + lane + 32 * i);
+                    }
+#pragma unroll
+                    for (uint32_t u = 0; u < 4; ++u) {
+                        if (cb + u > c_hi) break;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) v[i] += pv[u][i];
+                    }
                 }
                 if (lane == 0) sp.ticket[g] = 0;
             }
