@@ -108,6 +108,18 @@ __device__ __forceinline__ Geo phase_geo(const StepMat& m, uint32_t c, uint32_t 
 
 __device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
+// Atomic add with acquire and release semantics at gpu scope; returns the old value.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+// Add with release semantics at gpu scope (no result).
+__device__ __forceinline__ void red_add_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -421,6 +433,33 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
     }
 }
 
+// Bulk L2 prefetch of the K and V rows the CTA's attention items of layer l
+// will read (rows before `pos` already exist; the row at `pos` is written by
+// this step's qkv phase, in L2 by then).  Issued by one thread at the start of
+// the qkv phase, so that attention finds its rows in L2.
+template <typename KVT>
+__device__ void prefetch_attn_rows(const StepArgs& a, uint32_t l) {
+    const uint32_t row_bytes = a.hd * (uint32_t)sizeof(KVT);
+    if (row_bytes % 16) return;
+    const uint32_t c = min(a.st->pos + 1, a.max_seq), S = a.S_att;
+    const uint32_t Lk = (c + S - 1) / S;
+    const size_t layer_off = (size_t)l * a.KVH * a.max_seq * a.hd;
+    for (uint32_t it = blockIdx.x; it < a.KVH * S; it += gridDim.x) {
+        const uint32_t kvh = it / S, sidx = it % S;
+        const uint32_t t0 = sidx * Lk, t1 = min(c, t0 + Lk);
+        if (t1 <= t0) continue;
+        const size_t off = (layer_off + ((size_t)kvh * a.max_seq + t0) * a.hd) * sizeof(KVT);
+        const uint64_t bytes = (uint64_t)(t1 - t0) * row_bytes;
+        for (int kv = 0; kv < 2; ++kv) {
+            const uint8_t* base = static_cast<const uint8_t*>(kv ? a.vc : a.kc) + off;
+            for (uint64_t o = 0; o < bytes; o += 32768) {
+                const uint32_t n = (uint32_t)((bytes - o) < 32768 ? (bytes - o) : 32768);
+                bulk_prefetch_l2(base + o, n);
+            }
+        }
+    }
+}
+
 // ---------------------------------------------------------------- the step kernel
 
 template <int NV, int GQM, typename KVT>
@@ -516,12 +555,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
         const StepMat mt = phase_mat(a, p);
         step_prefetch_w(kind == kPhAttn ? nullptr : pro.w, mt.K, tid);  // before the barrier
         if (p > 0) {
-            if (tid == 0) {
-                wait_count(a.cnt + (p - 1), target, err);
-                __threadfence();
-            }
+            if (tid == 0) wait_count(a.cnt + (p - 1), target, err);  // acquire
             digit_sync();
         }
+        if (kind == kPhQKV && tid == 32 * 8) prefetch_attn_rows<KVT>(a, l);  // the finisher warp, before its first group
         if (kind == kPhAttn) {
             attn_phase<NV, GQM, KVT>(a, l, xb, tid);
             if (tid == 0) {
@@ -564,7 +601,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
 
         if (warp == kFinWarp) {
             // ---------------- finisher
+            const bool resid = kind == kPhO || kind == kPhDown;
             for (uint32_t g = gm.g_first; g <= gm.g_last; ++g) {
+                const uint32_t row0 = g * kTileRows;
+                float xv[4];  // residual input, loaded before the merge wait
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    xv[i] = (resid && row0 + lane + 32 * i < mt.M) ? __ldcg(a.x + row0 + lane + 32 * i) : 0.0f;
                 if (ok) ok = mbar_wait(&red_full[qs], qph, err);
                 float v[4];
 #pragma unroll
@@ -580,13 +623,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                     float* part = a.split_part + ((size_t)c * 2 + side) * kTileRows;
 #pragma unroll
                     for (int i = 0; i < 4; ++i) part[lane + 32 * i] = v[i];
-                    __threadfence();
                     __syncwarp();
-                    uint32_t last = 0;
-                    if (lane == 0) last = atomicAdd(a.split_ticket + g, 1u) == c_hi - c_lo;
+                    uint32_t last = 0;  // release our partial, acquire the others' (last arriver)
+                    if (lane == 0) last = atom_add_acq_rel_gpu(a.split_ticket + g, 1u) == c_hi - c_lo;
                     last = __shfl_sync(0xffffffffu, last, 0);
                     if (!last) continue;
-                    __threadfence();
 #pragma unroll
                     for (int i = 0; i < 4; ++i) v[i] = 0.0f;
                     for (uint32_t cb = c_lo; cb <= c_hi; cb += 8) {  // 8 CTAs' partials in flight, summed in CTA order
@@ -613,20 +654,25 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                 for (int i = 0; i < 4; ++i) fin[lane + 32 * i] = v[i];
                 __syncwarp();
                 auto rsf = [&](uint32_t t) { return fin[t]; };
-                const uint32_t row0 = g * kTileRows;
-                if (kind == kPhQKV) {
+                if (resid) {
+                    // x += y (transformer_engine.cpp:191-195, 222-225), optional per-layer tap
+                    float* tap = (kind == kPhDown && a.taps) ? a.taps + (size_t)l * a.D : nullptr;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t r = row0 + lane + 32 * i;
+                        if (r >= mt.M) continue;
+                        const float xn = __fadd_rn(xv[i], v[i]);
+                        a.x[r] = xn;
+                        if (tap) tap[r] = xn;
+                    }
+                } else if (kind == kPhQKV) {
                     EpiQKV<KVT> q{a.q,
                                   reinterpret_cast<KVT*>(a.kc) + (size_t)l * a.KVH * a.max_seq * a.hd,
                                   reinterpret_cast<KVT*>(a.vc) + (size_t)l * a.KVH * a.max_seq * a.hd,
                                   a.rope, a.st, a.D, a.KVD, a.hd, a.max_seq};
                     SEpiQKV<KVT>{q}.tile(est, row0, kTileRows, mt.M, lane, rsf);
-                } else if (kind == kPhO) {
-                    SEpiResidual{a.x, nullptr}.tile(est, row0, kTileRows, mt.M, lane, rsf);
                 } else if (kind == kPhGU) {
                     SEpiSwiGLU{a.act}.tile(est, row0, kTileRows, mt.M, lane, rsf);
-                } else if (kind == kPhDown) {
-                    SEpiResidual{a.x, a.taps ? a.taps + (size_t)l * a.D : nullptr}.tile(est, row0, kTileRows, mt.M,
-                                                                                         lane, rsf);
                 } else {
                     EpiLogits lg{a.logits, a.am_val, a.am_idx, a.am_ticket, a.st, a.tok_hist, a.max_seq};
                     SEpiLogits{lg}.tile(est, row0, kTileRows, mt.M, lane, rsf);
@@ -637,8 +683,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                 EpiLogits lg{a.logits, a.am_val, a.am_idx, a.am_ticket, a.st, a.tok_hist, a.max_seq, true};
                 SEpiLogits{lg}.end(est, lane);  // the last CTA advances the sequence (and its step count)
             } else if (lane == 0) {
-                __threadfence();
-                atomicAdd(a.cnt + p, 1u);
+                red_add_release_gpu(a.cnt + p, 1u);  // the warp's writes are ordered by the __syncwarp above
             }
             __syncwarp();
             continue;
