@@ -56,6 +56,8 @@ struct bt_engine {
     uint32_t step_nv = 0, step_ns = 0, step_xstride = 0, step_tmem = 0, step_scratch_off = 0;
     size_t step_smem = 0;
     StepLayer* d_layers = nullptr;  // device copy of the per-layer matrix table
+    uint8_t* step_img[2] = {nullptr, nullptr};  // digit images of GEMV inputs, by phase parity
+    float* step_ssp[2] = {nullptr, nullptr};    // row-tile sums of x^2, by phase parity
     uint32_t num_sms = 148;
     bool taps_on = false;
     std::vector<void*> allocs;
@@ -203,7 +205,8 @@ int plan_step(bt_engine* e) {
     e->step_nv = hd <= 64 ? 2 : hd <= 128 ? 4 : 8;
     e->step_ok = GQ * e->step_nv <= 16 && hd % e->step_nv == 0;
     const uint32_t kmax = c.dim > c.hidden_dim ? c.dim : c.hidden_dim;
-    size_t scratch = 2 * (size_t)mma_xstride(kmax);
+    const size_t img_bytes = 2 * (size_t)mma_xstride(kmax) + ((kmax / 32) * 4 + 15) / 16 * 16;  // digits + block scales
+    size_t scratch = img_bytes;
     const size_t attn = (size_t)kDigitWarps * GQ * (hd + 2) * 4;
     if (attn > scratch) scratch = attn;
     scratch = (scratch + 127) / 128 * 128;
@@ -232,6 +235,10 @@ int plan_step(bt_engine* e) {
         tab[l].ffn_norm = L.ffn_norm;
     }
     BT_TRY_ALLOC(e->allocs, &e->d_layers, c.num_layers, "step layer table");
+    for (int i = 0; i < 2; ++i) {
+        BT_TRY_ALLOC(e->allocs, &e->step_img[i], img_bytes, "step digit image");
+        BT_TRY_ALLOC(e->allocs, &e->step_ssp[i], (c.dim + kTileRows - 1) / kTileRows, "step norm partials");
+    }
     BT_CUDA_CHECK(cudaMemcpyAsync(e->d_layers, tab.data(), sizeof(StepLayer) * c.num_layers, cudaMemcpyHostToDevice,
                                   e->stream));
     BT_CUDA_CHECK(cudaStreamSynchronize(e->stream));
@@ -296,8 +303,13 @@ int launch_step(bt_engine* e, bt_kv* kv, cudaStream_t s) {
     a.att_part = kv->step_att_part;
     a.att_ticket = kv->step_att_ticket;
     a.cnt = kv->step_cnt;
+    for (int i = 0; i < 2; ++i) {
+        a.dimg[i] = e->step_img[i];
+        a.ssp[i] = e->step_ssp[i];
+    }
     a.L = c.num_layers;
     a.D = c.dim;
+    a.F = c.hidden_dim;
     a.KVD = kvd(c);
     a.hd = c.head_dim;
     a.KVH = c.num_kv_heads;

@@ -84,6 +84,10 @@ __device__ __forceinline__ void tmem_sync() { asm volatile("bar.sync 2, 256;" ::
 // async-proxy reads (tensor cores, bulk copies) of the same bytes.
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// Orders generic-proxy global accesses (including other SMs' writes this
+// thread has acquired) before this thread's later async-proxy global reads.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 // ---------------------------------------------------------------- tcgen05
 
 __device__ __forceinline__ void tcgen05_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }

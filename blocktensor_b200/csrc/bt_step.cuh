@@ -64,7 +64,9 @@ struct StepArgs {
     float* att_part;          // [KVH][GQ][S][hd + 2]
     uint32_t* att_ticket;     // [KVH]
     uint32_t* cnt;            // [5 L + 1] phase counters
-    uint32_t L, D, KVD, hd, KVH, GQ, max_seq, S_att;
+    uint8_t* dimg[2];         // digit images of GEMV inputs, by phase parity (layout of the shared digit area)
+    float* ssp[2];            // per-128-row-tile sums of x^2 of the next RMSNorm input, by phase parity
+    uint32_t L, D, KVD, F, hd, KVH, GQ, max_seq, S_att;
     float eps, scale;
     uint32_t NS, xstride, tmem_cols, scratch_off;
 };
@@ -143,18 +145,8 @@ struct MProStep {
     }
 };
 
-// Digits of the input of a GEMV phase (build_digits of bt_gemv_mma.cuh).  The
-// norm weights do not depend on earlier phases: step_prefetch_w pulls them
-// into L2 before the phase barrier, so after it the weight and activation
-// loads of step_build_digits share one round trip to L2.
-constexpr int kStepR = 6;  // items (8 elements) per digit thread held in registers: K <= 13824
-
-__device__ __forceinline__ void step_prefetch_w(const float* w, uint32_t K, uint32_t tid) {
-    if (!w) return;
-    for (uint32_t off = tid * 32; off < K; off += kDigitThreads * 32)  // one 128-byte line per thread
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(w + off));
-}
-
+// Elements of a GEMV phase's input: x (embedding row or activations through L2),
+// p = x * w with the RMSNorm weight w (or p = x), and the sums the norm needs.
 __device__ __forceinline__ float4 step_x(const MProStep& pro, const float* s, uint32_t k) {
     return pro.embed ? *reinterpret_cast<const float4*>(s + k) : ldcg4(s + k);
 }
@@ -175,69 +167,6 @@ __device__ __forceinline__ float4 step_p(const MProStep& pro, const float4& v, c
     return p;
 }
 
-__device__ int step_build_digits(const MProStep& pro, uint32_t K, uint8_t* xb, uint32_t xstride, float* red,
-                                 uint32_t tid, bool& bad) {
-    const float* s = pro.base(K);
-    const uint32_t items = K >> 3;
-    float ss = 0.0f, mx = 0.0f;
-    float4 pa[kStepR], pb[kStepR];
-    const float4 one = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
-#pragma unroll
-    for (int i = 0; i < kStepR; ++i) {
-        const uint32_t idx = tid + kDigitThreads * i;
-        if (idx < items) {
-            const uint32_t k = (idx >> 2) * 32 + (idx & 3) * 4;
-            const float4 xa = step_x(pro, s, k), xc = step_x(pro, s, k + 16);
-            const float4 ga = pro.w ? *reinterpret_cast<const float4*>(pro.w + k) : one;
-            const float4 gb = pro.w ? *reinterpret_cast<const float4*>(pro.w + k + 16) : one;
-            pa[i] = step_p(pro, xa, ga, k, ss, mx);
-            pb[i] = step_p(pro, xc, gb, k + 16, ss, mx);
-        }
-    }
-    for (uint32_t idx = tid + kDigitThreads * kStepR; idx < items; idx += kDigitThreads) {
-        const uint32_t k = (idx >> 2) * 32 + (idx & 3) * 4;
-        const float4 ga = pro.w ? *reinterpret_cast<const float4*>(pro.w + k) : one;
-        const float4 gb = pro.w ? *reinterpret_cast<const float4*>(pro.w + k + 16) : one;
-        step_p(pro, step_x(pro, s, k), ga, k, ss, mx);
-        step_p(pro, step_x(pro, s, k + 16), gb, k + 16, ss, mx);
-    }
-    ss = warp_sum(ss);
-    mx = warp_max(mx);
-    const uint32_t lane = tid & 31, w = tid >> 5;
-    if (lane == 0) { red[w] = ss; red[kDigitWarps + w] = mx; }
-    digit_sync();
-    float tss = 0.0f, tmx = 0.0f;
-#pragma unroll
-    for (int i = 0; i < kDigitWarps; ++i) { tss += red[i]; tmx = fmaxf(tmx, red[kDigitWarps + i]); }
-    const float f = pro.factor(tss, K);
-    const float m = tmx * f;
-    int e = 0;
-    bad = !isfinite(m);
-    if (m > 0.0f && !bad) {
-        int ex;
-        frexpf(m, &ex);
-        e = 21 - ex;
-    }
-    const float c1 = ldexpf(1.0f, e / 2), c2 = ldexpf(f, e - e / 2);
-#pragma unroll
-    for (int i = 0; i < kStepR; ++i) {
-        const uint32_t idx = tid + kDigitThreads * i;
-        if (idx < items) pack_item(xb, xstride, idx, pa[i], pb[i], c1, c2);
-    }
-    for (uint32_t idx = tid + kDigitThreads * kStepR; idx < items; idx += kDigitThreads) {
-        const uint32_t k = (idx >> 2) * 32 + (idx & 3) * 4;
-        float d0 = 0.0f, d1 = 0.0f;
-        const float4 ga = pro.w ? *reinterpret_cast<const float4*>(pro.w + k) : one;
-        const float4 gb = pro.w ? *reinterpret_cast<const float4*>(pro.w + k + 16) : one;
-        const float4 pa2 = step_p(pro, step_x(pro, s, k), ga, k, d0, d1);
-        const float4 pb2 = step_p(pro, step_x(pro, s, k + 16), gb, k + 16, d0, d1);
-        pack_item(xb, xstride, idx, pa2, pb2, c1, c2);
-    }
-    fence_proxy_async();
-    digit_sync();
-    return e;
-}
-
 // Waits (one thread) until cnt reaches target; bounded, and no wait at all
 // once an earlier wait of the step has timed out (*err set).
 __device__ __forceinline__ void wait_count(const uint32_t* cnt, uint32_t target, uint32_t* err) {
@@ -252,13 +181,133 @@ __device__ __forceinline__ void wait_count(const uint32_t* cnt, uint32_t target,
     }
 }
 
+// ---------------------------------------------------------------- digit images
+// The B operand of a GEMV phase, block by block: for block b (32 elements) of
+// the input, the signed base-256 digits (hi, mid, lo) of v = round(p * 2^e_b),
+// p the block's values (times the next RMSNorm weight) and e_b the block's own
+// exponent (max |p| * 2^e_b in [2^20, 2^21)), laid out as the shared digit
+// area: half c (elements 16c .. 16c+15) of digit row d at c * xstride + 48 b
+// + 16 d, then the block scales 2^-e_b (NaN for a block holding an inf or NaN)
+// as floats at 2 * xstride.  The RMSNorm factor is a per-vector scalar and is
+// applied to the GEMV results.  The warps that finalize a phase's values write
+// the next phase's image to global memory; the next phase fetches it with
+// bulk copies.
+
+__device__ __forceinline__ uint32_t blk_off(uint32_t xstride) { return 2 * xstride; }
+
+__device__ __forceinline__ int block_exponent(float am, bool& finite) {
+    finite = isfinite(am);
+    int e = 0;
+    if (am > 0.0f && finite) {
+        int ex;  // am = fr * 2^ex, fr in [0.5, 1)
+        if (am >= 1.17549435e-38f)
+            ex = ((__float_as_int(am) >> 23) & 255) - 126;
+        else
+            frexpf(am, &ex);
+        e = 21 - ex;
+        if (e > 149) e = 149;  // 2^-e stays representable
+    }
+    return e;
+}
+
+// 2^k for |k| <= 126, exactly.
+__device__ __forceinline__ float pow2i(int k) { return __int_as_float((127 + k) << 23); }
+
+// 2^-e for the block exponents above (subnormal below 2^-126).
+__device__ __forceinline__ float pow2neg(int e) { return e <= 126 ? pow2i(-e) : ldexpf(1.0f, -e); }
+
+// round(p * 2^e) for |p * 2^e| <= 2^21 (round half to even, as cvt.rni).
+__device__ __forceinline__ int scaled_round(float p, int e) {
+    const float t = __fmul_rn(__fmul_rn(p, pow2i(e / 2)), pow2i(e - e / 2));
+    return __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
+}
+
+// One warp, lane i holding element i of block b (warp-uniform call).
+__device__ __forceinline__ void warp_block_digits(uint8_t* img, uint32_t xstride, uint32_t b, float p, uint32_t lane) {
+    const float am = warp_max(fabsf(p));
+    bool finite;
+    const int e = block_exponent(am, finite);
+    const int v = finite ? scaled_round(p, e) : 0;
+    int dg[3];
+    digits3(v, dg[0], dg[1], dg[2]);
+    uint32_t word[3];
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+        const uint32_t by = (uint32_t)dg[d] & 255u;
+        word[d] = by | (__shfl_down_sync(0xffffffffu, by, 1) << 8) | (__shfl_down_sync(0xffffffffu, by, 2) << 16) |
+                  (__shfl_down_sync(0xffffffffu, by, 3) << 24);
+    }
+    if ((lane & 3) == 0) {
+        uint8_t* q = img + (lane >> 4) * xstride + b * 48 + (lane & 15);
+#pragma unroll
+        for (int d = 0; d < 3; ++d) *reinterpret_cast<uint32_t*>(q + 16 * d) = word[d];
+    }
+    if (lane == 0)
+        *reinterpret_cast<float*>(img + blk_off(xstride) + 4 * b) = finite ? pow2neg(e) : __int_as_float(0x7fc00000);
+}
+
+// A CTA builds the shared digit area of a whole input vector itself (the
+// embedding row of layer 0, or an input no finisher writes).  Digit threads
+// only; returns the RMSNorm factor (1 without a norm weight).
+__device__ float local_digits(const MProStep& pro, uint32_t K, uint8_t* xb, uint32_t xstride, float* red, uint32_t tid) {
+    const float* s = pro.base(K);
+    const uint32_t items = K >> 3;
+    const float4 one = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+    float ss = 0.0f;
+    for (uint32_t i0 = 0; i0 < items; i0 += kDigitThreads) {  // same trip count in every thread (shuffles below)
+        const uint32_t idx = i0 + tid;
+        const bool valid = idx < items;
+        const uint32_t k = (idx >> 2) * 32 + (idx & 3) * 4;
+        float4 pa = make_float4(0.f, 0.f, 0.f, 0.f), pb = pa;
+        float mx = 0.0f;
+        if (valid) {
+            const float4 ga = pro.w ? *reinterpret_cast<const float4*>(pro.w + k) : one;
+            const float4 gb = pro.w ? *reinterpret_cast<const float4*>(pro.w + k + 16) : one;
+            pa = step_p(pro, step_x(pro, s, k), ga, k, ss, mx);
+            pb = step_p(pro, step_x(pro, s, k + 16), gb, k + 16, ss, mx);
+        }
+        // the 4 items of a block are 4 consecutive lanes
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        bool finite;
+        const int e = block_exponent(mx, finite);
+        if (valid) {
+            pack_item(xb, xstride, idx, pa, pb, pow2i(e / 2), pow2i(e - e / 2));
+            if ((idx & 3) == 0)
+                *reinterpret_cast<float*>(xb + blk_off(xstride) + 4 * (idx >> 2)) =
+                    finite ? pow2neg(e) : __int_as_float(0x7fc00000);
+        }
+    }
+    ss = warp_sum(ss);
+    const uint32_t lane = tid & 31, w = tid >> 5;
+    if (lane == 0) red[w] = ss;
+    fence_proxy_async();  // generic-proxy writes -> visible to the tensor cores
+    digit_sync();
+    float tss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kDigitWarps; ++i) tss += red[i];
+    return pro.factor(tss, K);
+}
+
+// RMSNorm factor of a phase fed by a digit image: 1/sqrt(sum of the row-tile
+// sums of x^2 / K + eps), summed in a fixed order (one warp).
+__device__ __forceinline__ float image_inv(const float* ssp, uint32_t K, float eps, uint32_t lane) {
+    const uint32_t tiles = (K + kTileRows - 1) / kTileRows;
+    float ss = 0.0f;
+    for (uint32_t t = lane; t < tiles; t += 32) ss += __ldcg(ssp + t);
+    ss = warp_sum(ss);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
+}
+
 // ---------------------------------------------------------------- attention phase
 // Items (kv head, split) are dealt to the CTAs round robin; the 9 consumer
 // warps of a CTA take the item's keys round robin in batches (2 to 8 keys,
 // up to 64 bytes of K and V per lane, all loads of a batch in flight at once), with an online softmax per query head (lane i
 // holds head dims NV*i .. NV*i+NV-1), merge in shared memory, write the CTA's
 // partial (max m, sum l, o = sum e^(s-m) v), and the last CTA of a KV head
-// (ticket) merges the splits into attn (:148-184).
+// (ticket) merges the splits into attn (:148-184) and, with img (head_dim a
+// multiple of 32, so that blocks of 32 never straddle heads), writes the
+// o-proj input's digit image.
 
 // One lane's NV consecutive cache elements as 32-bit words, loaded through L2.
 template <int NV, typename KVT>
@@ -294,7 +343,7 @@ struct RowWords {
 };
 
 template <int NV, int GQM, typename KVT>
-__device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint32_t tid) {
+__device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint32_t tid, uint8_t* img) {
     // GQM: query heads per KV head held in registers; B: keys per batch and warp
     constexpr int BW = 16 / RowWords<NV, KVT>::W;
     constexpr int B = BW > 8 ? 8 : (BW < 2 ? 2 : BW);
@@ -425,7 +474,10 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
                         acc = fmaf(__ldcg(pb + s * pstride + 2 + d), f, acc);
                     }
                 }
-                a.attn[(size_t)(kvh * GQ + g) * HD + d] = __fdiv_rn(acc, lsum);
+                const float o = __fdiv_rn(acc, lsum);
+                a.attn[(size_t)(kvh * GQ + g) * HD + d] = o;
+                // digits of the o-proj input: this warp holds the 32 elements of one block
+                if (img) warp_block_digits(img, a.xstride, (kvh * GQ * HD + e) >> 5, o, lane);
             }
             if (tid == 0) a.att_ticket[kvh] = 0;
         }
@@ -467,6 +519,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[kMmaMaxRing], empty[kMmaMaxRing], mma_done[kMmaMaxRing];
     __shared__ __align__(8) uint64_t red_full[kRedSlots], red_free[kRedSlots];
+    __shared__ __align__(8) uint64_t dbar;  // digit image copies
     __shared__ float red[kRedSlots][kTileRows];
     __shared__ float fin[kTileRows];
     __shared__ float redd[2 * kDigitWarps];
@@ -489,6 +542,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
             mbar_init(&red_full[r], kAccWarps);
             mbar_init(&red_free[r], 1);
         }
+        mbar_init(&dbar, 1);
         fence_mbar_init();
     }
     if (warp == kMmaWarp0) {
@@ -530,52 +584,67 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
     const uint32_t tid = threadIdx.x - 32;
     const uint32_t epoch = a.st->pad[0];
     const uint32_t target = G * (epoch + 1);
+    const uint32_t pos = a.st->pos;  // changed only by the head phase's last CTA, at the very end
+    const uint32_t Dtiles = (a.D + kTileRows - 1) / kTileRows;
     bool ok = true;
     // per-role pipeline state, carried across phases
     uint32_t rs = 0, rph = 0;              // ring slot (issuers, accumulators)
     uint32_t qs = 0, qph = 0, qn = 0;      // reduction slot (accumulators, finisher) and slots used
+    uint32_t dph = 0;                      // digit-image barrier phase
     StreamState est{-INFINITY, 0xFFFFFFFFu};
     for (uint32_t p = 0; p < P; ++p) {
         const uint32_t kind = phase_kind(p, a.L);
         const uint32_t l = p / 5;
-        const StepLayer* ly = kind == kPhHead ? nullptr : a.layers + l;
-        MProStep pro{a.x, nullptr, a.eps, nullptr, a.st, a.x};
-        if (kind == kPhQKV) {
-            pro.w = ly->attn_norm;
-            if (l == 0) pro.embed = a.embed;
-        } else if (kind == kPhO) {
-            pro.src = a.attn;
-        } else if (kind == kPhGU) {
-            pro.w = ly->ffn_norm;
-        } else if (kind == kPhDown) {
-            pro.src = a.act;
-        } else if (kind == kPhHead) {
-            pro.w = a.out_norm;
-        }
         const StepMat mt = phase_mat(a, p);
-        step_prefetch_w(kind == kPhAttn ? nullptr : pro.w, mt.K, tid);  // before the barrier
         if (p > 0) {
             if (tid == 0) wait_count(a.cnt + (p - 1), target, err);  // acquire
             digit_sync();
         }
         if (kind == kPhQKV && tid == 32 * 8) prefetch_attn_rows<KVT>(a, l);  // the finisher warp, before its first group
+        uint8_t* img_next = a.dimg[(p + 1) & 1];
+        float* ssp_next = a.ssp[(p + 1) & 1];
         if (kind == kPhAttn) {
-            attn_phase<NV, GQM, KVT>(a, l, xb, tid);
+            attn_phase<NV, GQM, KVT>(a, l, xb, tid, a.hd % 32 == 0 ? img_next : nullptr);
             if (tid == 0) {
                 __threadfence();
-                atomicAdd(a.cnt + p, 1u);
+                red_add_release_gpu(a.cnt + p, 1u);
             }
             continue;
         }
         const Geo gm = phase_geo(mt, c, G);
-        bool bad = false;
-        const int e = step_build_digits(pro, mt.K, xb, a.xstride, redd, tid, bad);
+        const uint32_t NB = mt.K / kTileK;
+        const bool norm = kind == kPhQKV || kind == kPhGU || kind == kPhHead;
+        // the input's digits: a bulk copy of the image the previous phase wrote, or built here
+        const bool from_img = (kind == kPhQKV && l > 0) || kind == kPhGU || kind == kPhDown || kind == kPhHead ||
+                              (kind == kPhO && a.hd % 32 == 0);
+        float inv = 1.0f;
+        if (from_img) {
+            if (tid == 0) {
+                const uint8_t* src = a.dimg[p & 1];
+                const uint32_t hb = NB * 48 + 128, bb = (NB * 4 + 15) & ~15u;
+                fence_proxy_async_global();  // the image was written by generic stores of other SMs
+                mbar_expect_tx(&dbar, 2 * hb + bb);
+                bulk_g2s(xb, src, hb, &dbar);
+                bulk_g2s(xb + a.xstride, src + a.xstride, hb, &dbar);
+                bulk_g2s(xb + blk_off(a.xstride), src + blk_off(a.xstride), bb, &dbar);
+            }
+            if (ok) ok = mbar_wait(&dbar, dph, err);
+            dph ^= 1;
+        } else {
+            MProStep pro{kind == kPhO ? a.attn : a.x, nullptr, a.eps, nullptr, a.st, a.x};
+            if (kind == kPhQKV) {
+                pro.w = a.layers[l].attn_norm;
+                pro.embed = a.embed;  // layer 0
+            }
+            inv = local_digits(pro, mt.K, xb, a.xstride, redd, tid);
+        }
+        const float* blk = reinterpret_cast<const float*>(xb + blk_off(a.xstride));
 
         if (warp < kAccWarp0) {
             // ---------------- MMA issue
             const uint32_t t = warp - kMmaWarp0;
             if (lane == 0) {
-                uint32_t b = (gm.u0 + t) % gm.NB;
+                uint32_t b = (gm.u0 + t) % NB;
                 const uint64_t a0 = umma_desc(smem_u32(ring + t * kTileBytes), 128, 256);
                 const uint64_t b0 = umma_desc(smem_u32(xb), a.xstride, 128);
                 const uint32_t d0 = tmem + t * kTileCols;
@@ -589,7 +658,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                     umma_commit(&mma_done[s]);
                     if (++s == NS) { s = 0; ph ^= 1; }
                     b += kStageTiles;
-                    while (b >= gm.NB) b -= gm.NB;
+                    while (b >= NB) b -= NB;
                 }
             }
             // every issuer lane tracks the ring position
@@ -601,18 +670,40 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
 
         if (warp == kFinWarp) {
             // ---------------- finisher
+            if (norm && from_img) inv = image_inv(a.ssp[p & 1], mt.K, a.eps, lane);
             const bool resid = kind == kPhO || kind == kPhDown;
+            // the next RMSNorm's weight, for the digits of the next phase's input (residual phases)
+            const float* wnext = kind == kPhO ? a.layers[l].ffn_norm
+                                 : kind == kPhDown ? (l + 1 < a.L ? a.layers[l + 1].attn_norm : a.out_norm)
+                                                   : nullptr;
+            const uint32_t NBn = kind == kPhGU ? a.F / kTileK : a.D / kTileK;  // blocks of the next input
+            const uint32_t half = a.hd >> 1;
+            KVT* kl = reinterpret_cast<KVT*>(a.kc) + (size_t)l * a.KVH * a.max_seq * a.hd;
+            KVT* vl = reinterpret_cast<KVT*>(a.vc) + (size_t)l * a.KVH * a.max_seq * a.hd;
             for (uint32_t g = gm.g_first; g <= gm.g_last; ++g) {
                 const uint32_t row0 = g * kTileRows;
-                float xv[4];  // residual input, loaded before the merge wait
+                // epilogue inputs that do not depend on this phase, loaded before the merge wait
+                float xv[4], wv[4];
+                float2 cs[2];
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    xv[i] = (resid && row0 + lane + 32 * i < mt.M) ? __ldcg(a.x + row0 + lane + 32 * i) : 0.0f;
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t r = row0 + lane + 32 * i;
+                    xv[i] = (resid && r < mt.M) ? __ldcg(a.x + r) : 0.0f;
+                    wv[i] = (resid && r < mt.M) ? wnext[r] : 0.0f;
+                }
+                if (kind == kPhQKV) {
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        const uint32_t r = row0 + 2 * (lane + 32 * i);
+                        const uint32_t local = r < a.D ? r : r - a.D;
+                        cs[i] = (r < a.D + a.KVD && pos < a.max_seq) ? a.rope[(size_t)pos * half + ((local % a.hd) >> 1)]
+                                                                     : make_float2(1.0f, 0.0f);
+                    }
+                }
                 if (ok) ok = mbar_wait(&red_full[qs], qph, err);
                 float v[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    v[i] = bad ? __int_as_float(0x7fc00000) : ldexpf(red[qs][lane + 32 * i], -e);
+                for (int i = 0; i < 4; ++i) v[i] = red[qs][lane + 32 * i] * inv;
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&red_free[qs]);
                 if (++qs == kRedSlots) { qs = 0; qph ^= 1; }
@@ -650,32 +741,82 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                     }
                     if (lane == 0) a.split_ticket[g] = 0;
                 }
-#pragma unroll
-                for (int i = 0; i < 4; ++i) fin[lane + 32 * i] = v[i];
-                __syncwarp();
-                auto rsf = [&](uint32_t t) { return fin[t]; };
                 if (resid) {
-                    // x += y (transformer_engine.cpp:191-195, 222-225), optional per-layer tap
+                    // x += y (transformer_engine.cpp:191-195, 222-225), optional per-layer tap, then the
+                    // next phase's digits of x * w_next and this tile's sum of x^2
                     float* tap = (kind == kPhDown && a.taps) ? a.taps + (size_t)l * a.D : nullptr;
+                    float ss = 0.0f;
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const uint32_t r = row0 + lane + 32 * i;
-                        if (r >= mt.M) continue;
-                        const float xn = __fadd_rn(xv[i], v[i]);
-                        a.x[r] = xn;
-                        if (tap) tap[r] = xn;
+                        float xn = 0.0f;
+                        if (r < mt.M) {
+                            xn = __fadd_rn(xv[i], v[i]);
+                            a.x[r] = xn;
+                            if (tap) tap[r] = xn;
+                            ss = fmaf(xn, xn, ss);
+                        }
+                        if (4 * g + i < NBn) warp_block_digits(img_next, a.xstride, 4 * g + i, xn * wv[i], lane);
+                    }
+                    ss = warp_sum(ss);
+                    if (lane == 0) ssp_next[g] = ss;
+                } else if (kind == kPhGU) {
+                    // act = silu(gate) * up (cpu_ref.hpp:74-79, transformer_engine.cpp:212-215): rows (2j, 2j+1)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) fin[lane + 32 * i] = v[i];
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        const uint32_t pp = lane + 32 * i;
+                        const float gt = fin[2 * pp], up = fin[2 * pp + 1];
+                        float act = 0.0f;
+                        if (row0 + 2 * pp + 1 < mt.M) {
+                            act = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up);
+                            a.act[(row0 >> 1) + pp] = act;
+                        }
+                        if (2 * g + i < NBn) warp_block_digits(img_next, a.xstride, 2 * g + i, act, lane);
                     }
                 } else if (kind == kPhQKV) {
-                    EpiQKV<KVT> q{a.q,
-                                  reinterpret_cast<KVT*>(a.kc) + (size_t)l * a.KVH * a.max_seq * a.hd,
-                                  reinterpret_cast<KVT*>(a.vc) + (size_t)l * a.KVH * a.max_seq * a.hd,
-                                  a.rope, a.st, a.D, a.KVD, a.hd, a.max_seq};
-                    SEpiQKV<KVT>{q}.tile(est, row0, kTileRows, mt.M, lane, rsf);
-                } else if (kind == kPhGU) {
-                    SEpiSwiGLU{a.act}.tile(est, row0, kTileRows, mt.M, lane, rsf);
+                    // RoPE on (i, i + hd/2) pairs, q and the K/V append at pos (:117-146)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) fin[lane + 32 * i] = v[i];
+                    __syncwarp();
+                    if (pos < a.max_seq) {
+#pragma unroll
+                        for (int i = 0; i < 2; ++i) {
+                            const uint32_t pp = lane + 32 * i;
+                            const uint32_t r = row0 + 2 * pp;
+                            if (r >= mt.M) continue;
+                            const float x0 = fin[2 * pp], x1 = fin[2 * pp + 1];
+                            if (r < a.D + a.KVD) {
+                                const bool isq = r < a.D;
+                                const uint32_t local = isq ? r : r - a.D;
+                                const uint32_t h = local / a.hd, j = (local % a.hd) >> 1;
+                                const float o1 = __fsub_rn(__fmul_rn(x0, cs[i].x), __fmul_rn(x1, cs[i].y));
+                                const float o2 = __fadd_rn(__fmul_rn(x0, cs[i].y), __fmul_rn(x1, cs[i].x));
+                                if (isq) {
+                                    a.q[h * a.hd + j] = o1;
+                                    a.q[h * a.hd + j + half] = o2;
+                                } else {
+                                    KVT* dst = kl + ((size_t)h * a.max_seq + pos) * a.hd;
+                                    dst[j] = KVConv<KVT>::from_f(o1);
+                                    dst[j + half] = KVConv<KVT>::from_f(o2);
+                                }
+                            } else {
+                                const uint32_t local = r - a.D - a.KVD;
+                                const uint32_t h = local / a.hd, d = local % a.hd;
+                                KVT* dst = vl + ((size_t)h * a.max_seq + pos) * a.hd;
+                                dst[d] = KVConv<KVT>::from_f(x0);
+                                dst[d + 1] = KVConv<KVT>::from_f(x1);
+                            }
+                        }
+                    }
                 } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) fin[lane + 32 * i] = v[i];
+                    __syncwarp();
                     EpiLogits lg{a.logits, a.am_val, a.am_idx, a.am_ticket, a.st, a.tok_hist, a.max_seq};
-                    SEpiLogits{lg}.tile(est, row0, kTileRows, mt.M, lane, rsf);
+                    SEpiLogits{lg}.tile(est, row0, kTileRows, mt.M, lane, [&](uint32_t t) { return fin[t]; });
                 }
                 __syncwarp();
             }
@@ -706,7 +847,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                 if (++qs == kRedSlots) { qs = 0; qph ^= 1; }
                 ++cur_g;
             };
-            uint32_t g = gm.u0 / gm.NB, b = gm.u0 - g * gm.NB;
+            uint32_t g = gm.u0 / NB, b = gm.u0 - g * NB;
             for (uint32_t j = 0; j < gm.nstages; ++j) {
                 if (ok) ok = mbar_wait(&mma_done[rs], rph, err);
                 tcgen05_fence_after();
@@ -730,9 +871,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                         const uint32_t* dt = d + kTileCols * t;
                         const float y = fmaf(fmaf(small_i2f((int)dt[0]), 256.0f, small_i2f((int)dt[1])), 256.0f,
                                              small_i2f((int)dt[2]));
-                        acc = fmaf(sc[t], y, acc);
+                        acc = fmaf(sc[t] * blk[b], y, acc);  // weight scale x the block's 2^-e (read after the release)
                     }
-                    if (++b == gm.NB) { b = 0; ++g; }
+                    if (++b == NB) { b = 0; ++g; }
                 }
             }
             while (cur_g <= gm.g_last) flush();
