@@ -48,19 +48,20 @@ constexpr uint32_t kTileRows = 128;
 constexpr uint32_t kTileK = 32;
 constexpr uint32_t kTileQBytes = 4096;   // 128 x 32 int8
 constexpr uint32_t kTileBytes = 4608;    // + 128 fp32 scales
-constexpr uint32_t kStageTiles = 4;      // 18 KB stages
+constexpr uint32_t kStageTiles = 8;      // 36 KB stages
 constexpr uint32_t kStageBytes = kStageTiles * kTileBytes;
 constexpr uint32_t kTileCols = 8;        // TMEM columns per tile (N = 8)
 constexpr int kMmaThreads = 320;
 constexpr int kProducerWarp = 0;
 constexpr int kMmaWarp0 = 1;             // MMA issuers 1..4 (warp 1 owns the tensor memory)
+constexpr uint32_t kIssuers = 4;
 constexpr int kAccWarp0 = 5;             // accumulator warps 5..8
 constexpr int kAccWarps = 4;
 constexpr int kFinWarp = 9;
 constexpr int kDigitWarps = 9;           // warps 1..9
 constexpr int kDigitThreads = 32 * kDigitWarps;
 constexpr int kRedSlots = 4;
-constexpr uint32_t kMmaMaxRing = 16;     // stages (16 x 32 TMEM columns = 512)
+constexpr uint32_t kMmaMaxRing = 8;      // stages (8 x 64 TMEM columns = 512)
 
 // Instruction descriptor: D s32, A and B s8, both K-major, N = 8, M = 128.
 constexpr uint32_t kIdescS8 = (2u << 4) | (1u << 7) | (1u << 10) | ((8u >> 3) << 17) | ((128u >> 4) << 24);
@@ -375,6 +376,92 @@ struct SEpiLogits {
     }
 };
 
+// ---------------------------------------------------------------- MMA issue
+// Lane 0 of issuer warp t, one stage (n tiles, ring slot s): tiles t, t + 4,
+// ... of the stage.  a0/d0: the descriptor of tile t of slot 0 and its TMEM
+// columns; bt: the block index of tile t.  Descriptors advance by adding to
+// the start-address field (shared addresses < 256 KB: no carry).
+__device__ __forceinline__ void issue_stage(uint32_t t, uint32_t n, uint32_t s, uint32_t bt, uint32_t NB, uint64_t a0,
+                                            uint64_t b0, uint32_t d0) {
+#pragma unroll
+    for (uint32_t k = 0; k < kStageTiles / kIssuers; ++k) {
+        const uint32_t tt = t + k * kIssuers;
+        if (tt < n)
+            umma_s8(d0 + s * (kStageTiles * kTileCols) + k * kIssuers * kTileCols,
+                    a0 + ((s * kStageBytes + k * kIssuers * kTileBytes) >> 4), b0 + bt * 3, kIdescS8, 0);
+        bt += kIssuers;
+        while (bt >= NB) bt -= NB;
+    }
+}
+
+// ---------------------------------------------------------------- accumulator warp
+// Stages of an accumulator warp's loop handled together (their waits, tensor
+// memory loads and scale loads overlap).  Measured: 2 is slower than 1 (the
+// release of a stage then waits for the next stage's MMAs).
+constexpr uint32_t kAccBatch = 1;
+
+// Accumulator warp over tiles [u0, u1) in nstages stages: lane's row `row` of
+// every tile, y = (256 hi + mid) 256 + lo from the tile's three TMEM columns,
+// acc += scale(row, tile) * blk[block] * y.  blk: per-block factors (null: 1).
+// Before a tile of a new row tile, flush() hands acc on (and must zero it and
+// advance cur_g).  s/ph: the ring position, carried by the caller.
+template <class Flush>
+__device__ __forceinline__ void acc_stages(uint32_t u0, uint32_t u1, uint32_t NB, uint32_t nstages, const uint8_t* ring,
+                                           uint32_t NS, uint32_t taddr, uint32_t row, const float* blk,
+                                           uint64_t* mma_done, uint64_t* empty, uint32_t& s, uint32_t& ph, bool& ok,
+                                           uint32_t* err, float& acc, uint32_t& cur_g, Flush flush) {
+    const uint32_t lane = threadIdx.x & 31;
+    uint32_t g = NB ? u0 / NB : 0, b = u0 - g * NB;  // row tile and block of the next tile
+    for (uint32_t j = 0; j < nstages; j += kAccBatch) {
+        const uint32_t m = min(kAccBatch, nstages - j);  // stages in this batch (warp-uniform)
+        uint32_t d[kAccBatch][kStageTiles * kTileCols];
+        float sc[kAccBatch][kStageTiles];
+        uint32_t sl[kAccBatch], nt[kAccBatch];
+#pragma unroll
+        for (uint32_t k = 0; k < kAccBatch; ++k) {
+            sl[k] = s;
+            nt[k] = 0;
+            if (k < m) {
+                if (ok) ok = mbar_wait(&mma_done[s], ph, err);
+                tcgen05_fence_after();
+                tmem_ld64(taddr + s * (kStageTiles * kTileCols), d[k]);
+                nt[k] = min(kStageTiles, u1 - (u0 + (j + k) * kStageTiles));
+                const uint8_t* st = ring + (size_t)s * kStageBytes + kTileQBytes + row * 4;
+#pragma unroll
+                for (uint32_t t = 0; t < kStageTiles; ++t)
+                    sc[k][t] = t < nt[k] ? *reinterpret_cast<const float*>(st + t * kTileBytes) : 0.0f;
+                if (++s == NS) { s = 0; ph ^= 1; }
+            }
+        }
+        tmem_wait_ld();
+        tcgen05_fence_before();
+        __syncwarp();
+        if (lane == 0)
+            for (uint32_t k = 0; k < m; ++k) mbar_arrive(&empty[sl[k]]);  // stages (smem and TMEM columns) free
+#pragma unroll
+        for (uint32_t k = 0; k < kAccBatch; ++k) {
+            if (k >= m) break;
+            // block factors (read after the release) and digit sums before the first possible flush
+            float y[kStageTiles], bs[kStageTiles];
+#pragma unroll
+            for (uint32_t t = 0, bt = b; t < kStageTiles; ++t) {
+                const uint32_t* dt = d[k] + kTileCols * t;  // columns hi, mid, lo of tile t
+                y[t] = fmaf(fmaf(small_i2f((int)dt[0]), 256.0f, small_i2f((int)dt[1])), 256.0f, small_i2f((int)dt[2]));
+                bs[t] = blk ? blk[bt] : 1.0f;
+                if (++bt == NB) bt = 0;
+            }
+#pragma unroll
+            for (uint32_t t = 0; t < kStageTiles; ++t) {
+                if (t < nt[k]) {
+                    while (cur_g < g) flush();
+                    acc = fmaf(sc[k][t] * bs[t], y[t], acc);  // weight scale x the block's factor
+                }
+                if (++b == NB) { b = 0; ++g; }
+            }
+        }
+    }
+}
+
 // ---------------------------------------------------------------- kernel
 
 // The next GEMV of the sequence: the producer prefetches into L2 the first
@@ -419,7 +506,7 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
         for (uint32_t s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kAccWarps);
-            mbar_init(&mma_done[s], kStageTiles);  // one commit per issuer
+            mbar_init(&mma_done[s], kIssuers);  // one commit per issuer
         }
         for (int r = 0; r < kRedSlots; ++r) {
             mbar_init(&red_full[r], kAccWarps);
@@ -474,7 +561,7 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
     const int e = build_digits(pro, K, xb, sh.xstride, redd, threadIdx.x - 32, bad);
 
     if (warp < kAccWarp0) {
-        // ---------------- MMA issue: lane 0 of warp 1+t issues tile t of every stage
+        // ---------------- MMA issue: lane 0 of warp 1+t issues tiles t, t+4 of every stage
         const uint32_t t = warp - kMmaWarp0;
         if (lane == 0) {
             bool ok = true;
@@ -486,8 +573,7 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
             for (uint32_t j = 0; j < nstages; ++j) {
                 if (ok) ok = mbar_wait(&full[s], ph, err);
                 tcgen05_fence_after();
-                if (ok && t < min(kStageTiles, u1 - (u0 + j * kStageTiles)))
-                    umma_s8(d0 + s * (kStageTiles * kTileCols), a0 + ((s * kStageBytes) >> 4), b0 + b * 3, kIdescS8, 0);
+                if (ok) issue_stage(t, min(kStageTiles, u1 - (u0 + j * kStageTiles)), s, b, NB, a0, b0, d0);
                 umma_commit(&mma_done[s]);  // arrives once this issuer's MMAs are complete
                 if (++s == NS) { s = 0; ph ^= 1; }
                 b += kStageTiles;
@@ -581,36 +667,8 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
         if (++rslot == kRedSlots) { rslot = 0; rph ^= 1; }
         ++cur_g;
     };
-    uint32_t g = u0 / NB, b = u0 - g * NB;  // row tile and block of the next tile
     uint32_t s = 0, ph = 0;
-    for (uint32_t j = 0; j < nstages; ++j) {
-        if (ok) ok = mbar_wait(&mma_done[s], ph, err);
-        tcgen05_fence_after();
-        uint32_t d[32];
-        tmem_ld32(taddr + s * (kStageTiles * kTileCols), d);
-        const uint32_t n = min(kStageTiles, u1 - (u0 + j * kStageTiles));
-        const uint8_t* st = ring + (size_t)s * kStageBytes + kTileQBytes + row * 4;
-        float sc[kStageTiles];
-#pragma unroll
-        for (uint32_t t = 0; t < kStageTiles; ++t)
-            sc[t] = t < n ? *reinterpret_cast<const float*>(st + t * kTileBytes) : 0.0f;
-        tmem_wait_ld();
-        tcgen05_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);  // stage (smem and TMEM columns) free
-        if (++s == NS) { s = 0; ph ^= 1; }
-#pragma unroll
-        for (uint32_t t = 0; t < kStageTiles; ++t) {
-            if (t < n) {
-                while (cur_g < g) flush();
-                const uint32_t* dt = d + kTileCols * t;  // columns hi, mid, lo of tile t
-                const float y = fmaf(fmaf(small_i2f((int)dt[0]), 256.0f, small_i2f((int)dt[1])), 256.0f,
-                                     small_i2f((int)dt[2]));
-                acc = fmaf(sc[t], y, acc);
-            }
-            if (++b == NB) { b = 0; ++g; }
-        }
-    }
+    acc_stages(u0, u1, NB, nstages, ring, NS, taddr, row, nullptr, mma_done, empty, s, ph, ok, err, acc, cur_g, flush);
     while (cur_g <= g_last) flush();
     tcgen05_fence_before();
     tmem_sync();
@@ -626,7 +684,7 @@ inline size_t mma_smem(const MmaShape& sh, uint32_t K) {
     return need > 80 * 1024 ? need : 80 * 1024;
 }
 
-// Ring of about ring_bytes (2..16 stages); one CTA per SM (at most U).
+// Ring of about ring_bytes (2..8 stages); one CTA per SM (at most U).
 inline bool mma_plan(uint32_t Mp, uint32_t K, uint32_t nsm, uint32_t ring_bytes, MmaShape& sh, uint32_t& grid) {
     if (K % kTileK || Mp % kTileRows || Mp == 0 || K == 0) return false;
     uint32_t ns = ring_bytes / kStageBytes;
@@ -642,11 +700,11 @@ inline bool mma_plan(uint32_t Mp, uint32_t K, uint32_t nsm, uint32_t ring_bytes,
     return mma_smem(sh, K) <= 220 * 1024 && (cols <= 256 || mma_smem(sh, K) > 114 * 1024);
 }
 
-// Default ring: about 150 KB of shared memory per CTA (one CTA per SM).
+// Default ring: about 200 KB of shared memory per CTA (one CTA per SM).
 // Measured on the 7B decode step, a deep ring beats two co-resident CTAs with
 // half the ring each (the next GEMV then streams under programmatic dependent
 // launch, but every GEMV has half the bytes in flight).
-constexpr uint32_t kMmaCoResidentDyn = 150 * 1024;
+constexpr uint32_t kMmaCoResidentDyn = 200 * 1024;
 
 inline uint32_t mma_ring_bytes(uint32_t K) {
     static int env_kb = -1;

@@ -536,7 +536,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
         for (uint32_t s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kAccWarps);
-            mbar_init(&mma_done[s], kStageTiles);
+            mbar_init(&mma_done[s], kIssuers);
         }
         for (int r = 0; r < kRedSlots; ++r) {
             mbar_init(&red_full[r], kAccWarps);
@@ -652,9 +652,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                 for (uint32_t j = 0; j < gm.nstages; ++j) {
                     if (ok) ok = mbar_wait(&full[s], ph, err);
                     tcgen05_fence_after();
-                    if (ok && t < min(kStageTiles, gm.u1 - (gm.u0 + j * kStageTiles)))
-                        umma_s8(d0 + s * (kStageTiles * kTileCols), a0 + ((s * kStageBytes) >> 4), b0 + b * 3,
-                                kIdescS8, 0);
+                    if (ok) issue_stage(t, min(kStageTiles, gm.u1 - (gm.u0 + j * kStageTiles)), s, b, NB, a0, b0, d0);
                     umma_commit(&mma_done[s]);
                     if (++s == NS) { s = 0; ph ^= 1; }
                     b += kStageTiles;
@@ -847,35 +845,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                 if (++qs == kRedSlots) { qs = 0; qph ^= 1; }
                 ++cur_g;
             };
-            uint32_t g = gm.u0 / NB, b = gm.u0 - g * NB;
-            for (uint32_t j = 0; j < gm.nstages; ++j) {
-                if (ok) ok = mbar_wait(&mma_done[rs], rph, err);
-                tcgen05_fence_after();
-                uint32_t d[32];
-                tmem_ld32(taddr + rs * (kStageTiles * kTileCols), d);
-                const uint32_t n = min(kStageTiles, gm.u1 - (gm.u0 + j * kStageTiles));
-                const uint8_t* st = ring + (size_t)rs * kStageBytes + kTileQBytes + row * 4;
-                float sc[kStageTiles];
-#pragma unroll
-                for (uint32_t t = 0; t < kStageTiles; ++t)
-                    sc[t] = t < n ? *reinterpret_cast<const float*>(st + t * kTileBytes) : 0.0f;
-                tmem_wait_ld();
-                tcgen05_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[rs]);
-                if (++rs == NS) { rs = 0; rph ^= 1; }
-#pragma unroll
-                for (uint32_t t = 0; t < kStageTiles; ++t) {
-                    if (t < n) {
-                        while (cur_g < g) flush();
-                        const uint32_t* dt = d + kTileCols * t;
-                        const float y = fmaf(fmaf(small_i2f((int)dt[0]), 256.0f, small_i2f((int)dt[1])), 256.0f,
-                                             small_i2f((int)dt[2]));
-                        acc = fmaf(sc[t] * blk[b], y, acc);  // weight scale x the block's 2^-e (read after the release)
-                    }
-                    if (++b == NB) { b = 0; ++g; }
-                }
-            }
+            acc_stages(gm.u0, gm.u1, NB, gm.nstages, ring, NS, taddr, row, blk, mma_done, empty, rs, rph, ok, err, acc,
+                       cur_g, flush);
             while (cur_g <= gm.g_last) flush();
         }
     }
