@@ -65,7 +65,8 @@ struct bt_engine {
     float* embed = nullptr;
     float* out_norm = nullptr;
     uint8_t* head = nullptr;  // V x D units
-    // partial sums of row tiles cut between CTAs of a GEMV ([num_sms][2][128]) + one ticket per row tile
+    // partial sums of row tiles cut between CTAs of a GEMV ([num_sms][2][128] floats, or 64-bit tagged
+    // words in the step kernel) + one ticket per row tile (standalone GEMVs)
     float* split_part = nullptr;
     uint32_t* split_ticket = nullptr;
     // activations
@@ -203,7 +204,8 @@ int plan_step(bt_engine* e) {
     const auto& c = e->cfg;
     const uint32_t hd = c.head_dim, GQ = c.num_heads / c.num_kv_heads;
     e->step_nv = hd <= 64 ? 2 : hd <= 128 ? 4 : 8;
-    e->step_ok = GQ * e->step_nv <= 16 && hd % e->step_nv == 0;
+    // phases 5 L + 1 < 1024: the phase index is the low 10 bits of the split partials' tags
+    e->step_ok = GQ * e->step_nv <= 16 && hd % e->step_nv == 0 && 5 * c.num_layers + 1 < 1024;
     const uint32_t kmax = c.dim > c.hidden_dim ? c.dim : c.hidden_dim;
     const size_t img_bytes = 2 * (size_t)mma_xstride(kmax) + ((kmax / 32) * 4 + 15) / 16 * 16;  // digits + block scales
     size_t scratch = img_bytes;
@@ -295,8 +297,7 @@ int launch_step(bt_engine* e, bt_kv* kv, cudaStream_t s) {
     a.rope = kv->rope;
     a.st = kv->st;
     a.tok_hist = kv->tok_hist;
-    a.split_part = e->split_part;
-    a.split_ticket = e->split_ticket;
+    a.split_part = reinterpret_cast<uint64_t*>(e->split_part);
     a.am_val = e->am_val;
     a.am_idx = e->am_idx;
     a.am_ticket = e->am_ticket;
@@ -378,7 +379,9 @@ int alloc_weights(bt_engine* e) {
     if (2 * F > rows) rows = (uint32_t)(2 * F);
     if (D + 2 * KV > rows) rows = (uint32_t)(D + 2 * KV);
     const size_t tickets = mma_row_tiles(unit_rows(rows));
-    BT_TRY_ALLOC(A, &e->split_part, (size_t)e->num_sms * 2 * kTileRows, "split partials");
+    // floats for the standalone GEMVs; (tag, value) words for the step kernel, zeroed (tag 0 is never valid)
+    BT_TRY_ALLOC(A, &e->split_part, (size_t)e->num_sms * 2 * kTileRows * 2, "split partials");
+    BT_CUDA_CHECK(cudaMemsetAsync(e->split_part, 0, sizeof(float) * e->num_sms * 2 * kTileRows * 2, e->stream));
     BT_TRY_ALLOC(A, &e->split_ticket, tickets, "split tickets");
     BT_CUDA_CHECK(cudaMemsetAsync(e->split_ticket, 0, sizeof(uint32_t) * tickets, e->stream));
     return plan_step(e);

@@ -202,7 +202,9 @@ struct EpiLogits {
     DevState* st;
     uint32_t* tok_hist;  // [max_seq + 1]
     uint32_t max_seq;
-    bool bump_epoch = false;  // the last CTA also counts the step in st->pad[0] (persistent step kernel)
+    // persistent step kernel: the last CTA also counts the step in st->pad[0] and
+    // the engine's step launches in ticket[1] (the tag of its split partials)
+    bool bump_epoch = false;
     template <int ROWS>
     __device__ void finish(const float* yr, uint32_t row0, uint32_t M) const {
         __shared__ bool s_last;

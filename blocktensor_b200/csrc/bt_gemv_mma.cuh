@@ -370,7 +370,10 @@ struct SEpiLogits {
             st->last_argmax = ix;
             st->cur_token = next;
             st->pos = pos + 1;
-            if (e.bump_epoch) st->pad[0] += 1;
+            if (e.bump_epoch) {
+                st->pad[0] += 1;
+                e.ticket[1] += 1;
+            }
             *e.ticket = 0;
         }
     }

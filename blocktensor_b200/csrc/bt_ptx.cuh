@@ -182,6 +182,18 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&d)[64]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 64-bit accesses that are single-copy atomic and morally strong at gpu scope
+// (a value and its tag published together, read by another SM's poll).
+__device__ __forceinline__ void st_relaxed_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Exact int -> float for |v| < 2^22 with two full-rate ops.
 __device__ __forceinline__ float small_i2f(int v) {
     return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);

@@ -56,8 +56,7 @@ struct StepArgs {
     const float2* rope;       // [max_seq][hd/2]
     DevState* st;
     uint32_t* tok_hist;
-    float* split_part;        // [G][2][128]
-    uint32_t* split_ticket;   // [row tiles of the tallest matrix]
+    uint64_t* split_part;     // [G][2][128] tagged partial sums: (tag << 32) | float bits
     float* am_val;            // [G]
     uint32_t* am_idx;
     uint32_t* am_ticket;
@@ -222,25 +221,31 @@ __device__ __forceinline__ int scaled_round(float p, int e) {
     return __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
 }
 
-// One warp, lane i holding element i of block b (warp-uniform call).
+// One warp, lane i holding element i of block b (warp-uniform call).  The
+// block's max |p| is one redux.sync on the bit patterns (monotonic for
+// non-negative floats; an inf or NaN anywhere makes the block's scale NaN, so
+// it propagates to every output as in fp32 arithmetic); each lane packs its
+// three digit bytes into one word and three shuffles bring the next lanes'
+// words for the 4-element digit words of lanes 0, 4, ... .
 __device__ __forceinline__ void warp_block_digits(uint8_t* img, uint32_t xstride, uint32_t b, float p, uint32_t lane) {
-    const float am = warp_max(fabsf(p));
+    const float am = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(p))));
     bool finite;
     const int e = block_exponent(am, finite);
     const int v = finite ? scaled_round(p, e) : 0;
-    int dg[3];
-    digits3(v, dg[0], dg[1], dg[2]);
-    uint32_t word[3];
-#pragma unroll
-    for (int d = 0; d < 3; ++d) {
-        const uint32_t by = (uint32_t)dg[d] & 255u;
-        word[d] = by | (__shfl_down_sync(0xffffffffu, by, 1) << 8) | (__shfl_down_sync(0xffffffffu, by, 2) << 16) |
-                  (__shfl_down_sync(0xffffffffu, by, 3) << 24);
-    }
+    int hi, mid, lo;
+    digits3(v, hi, mid, lo);
+    const uint32_t w0 = ((uint32_t)hi & 255u) | (((uint32_t)mid & 255u) << 8) | (((uint32_t)lo & 255u) << 16);
+    const uint32_t w1 = __shfl_down_sync(0xffffffffu, w0, 1);
+    const uint32_t w2 = __shfl_down_sync(0xffffffffu, w0, 2);
+    const uint32_t w3 = __shfl_down_sync(0xffffffffu, w0, 3);
     if ((lane & 3) == 0) {
+        // digit d of elements lane .. lane+3: byte d of w0, w1, w2, w3
+        const uint32_t a01 = __byte_perm(w0, w1, 0x5140), a23 = __byte_perm(w2, w3, 0x5140);  // hi, mid bytes
+        const uint32_t b01 = __byte_perm(w0, w1, 0x0062), b23 = __byte_perm(w2, w3, 0x0062);  // lo bytes
         uint8_t* q = img + (lane >> 4) * xstride + b * 48 + (lane & 15);
-#pragma unroll
-        for (int d = 0; d < 3; ++d) *reinterpret_cast<uint32_t*>(q + 16 * d) = word[d];
+        *reinterpret_cast<uint32_t*>(q) = __byte_perm(a01, a23, 0x5410);        // hi
+        *reinterpret_cast<uint32_t*>(q + 16) = __byte_perm(a01, a23, 0x7632);   // mid
+        *reinterpret_cast<uint32_t*>(q + 32) = __byte_perm(b01, b23, 0x5410);   // lo
     }
     if (lane == 0)
         *reinterpret_cast<float*>(img + blk_off(xstride) + 4 * b) = finite ? pow2neg(e) : __int_as_float(0x7fc00000);
@@ -585,6 +590,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
     const uint32_t epoch = a.st->pad[0];
     const uint32_t target = G * (epoch + 1);
     const uint32_t pos = a.st->pos;  // changed only by the head phase's last CTA, at the very end
+    const uint32_t launch = a.am_ticket[1];  // step launches of the engine so far (bumped at the very end)
     const uint32_t Dtiles = (a.D + kTileRows - 1) / kTileRows;
     bool ok = true;
     // per-role pipeline state, carried across phases
@@ -675,6 +681,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                                  : kind == kPhDown ? (l + 1 < a.L ? a.layers[l + 1].attn_norm : a.out_norm)
                                                    : nullptr;
             const uint32_t NBn = kind == kPhGU ? a.F / kTileK : a.D / kTileK;  // blocks of the next input
+            // tag of this launch's phase-p partials: never 0, never a value of another launch or phase
+            const uint32_t tag = ((launch + 1) << 10) | p;
             const uint32_t half = a.hd >> 1;
             KVT* kl = reinterpret_cast<KVT*>(a.kc) + (size_t)l * a.KVH * a.max_seq * a.hd;
             KVT* vl = reinterpret_cast<KVT*>(a.vc) + (size_t)l * a.KVH * a.max_seq * a.hd;
@@ -708,36 +716,47 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                 const uint32_t c_lo = split_cta((uint64_t)g * gm.NB, gm.U, gm.Gm);
                 const uint32_t c_hi = split_cta((uint64_t)(g + 1) * gm.NB - 1, gm.U, gm.Gm);
                 if (c_lo != c_hi) {
-                    const uint32_t side = g == gm.g_first ? 0 : 1;
-                    float* part = a.split_part + ((size_t)c * 2 + side) * kTileRows;
+                    if (c != c_lo) {
+                        // publish this piece for CTA c_lo (value and tag in one 64-bit word) and move on
+                        uint64_t* part = a.split_part + ((size_t)c * 2 + (g == gm.g_first ? 0 : 1)) * kTileRows;
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) part[lane + 32 * i] = v[i];
-                    __syncwarp();
-                    uint32_t last = 0;  // release our partial, acquire the others' (last arriver)
-                    if (lane == 0) last = atom_add_acq_rel_gpu(a.split_ticket + g, 1u) == c_hi - c_lo;
-                    last = __shfl_sync(0xffffffffu, last, 0);
-                    if (!last) continue;
+                        for (int i = 0; i < 4; ++i)
+                            st_relaxed_u64(part + lane + 32 * i, ((uint64_t)tag << 32) | __float_as_uint(v[i]));
+                        continue;
+                    }
+                    // CTA c_lo finishes the row tile (its own piece is its range's last): add the other
+                    // pieces in CTA order once their tags say they are this phase's
+                    for (uint32_t cb = c_lo + 1; cb <= c_hi && ok; cb += 4) {
+                        uint64_t pv[4][4];
+                        const uint64_t t0 = global_ns();
+                        while (true) {
+                            bool have = true;
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) v[i] = 0.0f;
-                    for (uint32_t cb = c_lo; cb <= c_hi; cb += 8) {  // 8 CTAs' partials in flight, summed in CTA order
-                        float pv[8][4];
+                            for (uint32_t u = 0; u < 4; ++u) {
+                                const uint32_t cc = cb + u;
+                                if (cc > c_hi) break;
+                                const uint32_t first_cc = (uint32_t)(((uint64_t)gm.U * cc) / gm.Gm) / gm.NB;
+                                const uint64_t* pc = a.split_part + ((size_t)cc * 2 + (g == first_cc ? 0 : 1)) * kTileRows;
 #pragma unroll
-                        for (uint32_t u = 0; u < 8; ++u) {
-                            const uint32_t cc = cb + u;
-                            if (cc > c_hi) break;
-                            const uint32_t first_cc = (uint32_t)(((uint64_t)gm.U * cc) / gm.Gm) / gm.NB;
-                            const float* pc = a.split_part + ((size_t)cc * 2 + (g == first_cc ? 0 : 1)) * kTileRows;
-#pragma unroll
-                            for (int i = 0; i < 4; ++i) pv[u][i] = __ldcg(pc + lane + 32 * i);
+                                for (int i = 0; i < 4; ++i) {
+                                    pv[u][i] = ld_relaxed_u64(pc + lane + 32 * i);
+                                    have = have && (uint32_t)(pv[u][i] >> 32) == tag;
+                                }
+                            }
+                            if (__all_sync(0xffffffffu, have)) break;
+                            if (global_ns() - t0 > kWaitNs) {
+                                if (lane == 0) atomicExch(err, 1u);
+                                ok = false;
+                                break;
+                            }
                         }
 #pragma unroll
-                        for (uint32_t u = 0; u < 8; ++u) {
+                        for (uint32_t u = 0; u < 4; ++u) {
                             if (cb + u > c_hi) break;
 #pragma unroll
-                            for (int i = 0; i < 4; ++i) v[i] += pv[u][i];
+                            for (int i = 0; i < 4; ++i) v[i] += __uint_as_float((uint32_t)pv[u][i]);
                         }
                     }
-                    if (lane == 0) a.split_ticket[g] = 0;
                 }
                 if (resid) {
                     // x += y (transformer_engine.cpp:191-195, 222-225), optional per-layer tap, then the
