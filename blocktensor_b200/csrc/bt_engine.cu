@@ -103,8 +103,7 @@ struct bt_kv {
     bool graph_taps = false;
     // persistent step kernel: phase counters [5 L + 1], attention split partials and tickets
     uint32_t* step_cnt = nullptr;
-    float* step_att_part = nullptr;
-    uint32_t* step_att_ticket = nullptr;
+    uint64_t* step_att_part = nullptr;  // tagged attention split partials of the step kernel
     uint32_t step_S = 1;
 };
 
@@ -302,7 +301,6 @@ int launch_step(bt_engine* e, bt_kv* kv, cudaStream_t s) {
     a.am_idx = e->am_idx;
     a.am_ticket = e->am_ticket;
     a.att_part = kv->step_att_part;
-    a.att_ticket = kv->step_att_ticket;
     a.cnt = kv->step_cnt;
     for (int i = 0; i < 2; ++i) {
         a.dimg[i] = e->step_img[i];
@@ -769,20 +767,23 @@ int bt_kv_create(bt_engine* e, uint32_t max_seq, int dtype, bt_kv** out) {
         return cleanup(rc);
     if ((rc = dev_alloc(kv->allocs, &kv->att_ticket, (size_t)c.num_layers * c.num_kv_heads, "attention tickets")))
         return cleanup(rc);
-    // persistent step kernel: one attention item per (KV head, split), about one per SM
+    // persistent step kernel: one attention item per (KV head, split), about one per SM, at most
+    // kAttnMaxSplits splits per head (split 0's CTA holds them all in registers when it merges)
     kv->step_S = e->num_sms / c.num_kv_heads;
     if (kv->step_S < 1) kv->step_S = 1;
+    if (kv->step_S > kAttnMaxSplits) kv->step_S = kAttnMaxSplits;
     const uint32_t GQ = c.num_heads / c.num_kv_heads;
     if ((rc = dev_alloc(kv->allocs, &kv->step_cnt, (size_t)5 * c.num_layers + 1, "phase counters")))
         return cleanup(rc);
     if ((rc = dev_alloc(kv->allocs, &kv->step_att_part,
                         (size_t)c.num_kv_heads * GQ * kv->step_S * (c.head_dim + 2), "step attention partials")))
         return cleanup(rc);
-    if ((rc = dev_alloc(kv->allocs, &kv->step_att_ticket, c.num_kv_heads, "step attention tickets")))
-        return cleanup(rc);
     cudaError_t ce = cudaMemsetAsync(kv->att_ticket, 0, sizeof(uint32_t) * c.num_layers * c.num_kv_heads, e->stream);
     if (ce == cudaSuccess) ce = cudaMemsetAsync(kv->step_cnt, 0, sizeof(uint32_t) * (5 * c.num_layers + 1), e->stream);
-    if (ce == cudaSuccess) ce = cudaMemsetAsync(kv->step_att_ticket, 0, sizeof(uint32_t) * c.num_kv_heads, e->stream);
+    // tag 0 is never a valid tag: zeroed partials are never taken for a split's
+    if (ce == cudaSuccess)
+        ce = cudaMemsetAsync(kv->step_att_part, 0,
+                             sizeof(uint64_t) * c.num_kv_heads * GQ * kv->step_S * (c.head_dim + 2), e->stream);
     if (ce == cudaSuccess) ce = cudaMemsetAsync(kb, 0, n * esz, e->stream);
     if (ce == cudaSuccess) ce = cudaMemsetAsync(vb, 0, n * esz, e->stream);
     if (ce == cudaSuccess) ce = cudaMemsetAsync(kv->st, 0, sizeof(DevState), e->stream);

@@ -60,8 +60,7 @@ struct StepArgs {
     float* am_val;            // [G]
     uint32_t* am_idx;
     uint32_t* am_ticket;
-    float* att_part;          // [KVH][GQ][S][hd + 2]
-    uint32_t* att_ticket;     // [KVH]
+    uint64_t* att_part;       // [KVH][GQ][S][hd + 2] tagged (m, l, o) of the splits (S <= kAttnMaxSplits)
     uint32_t* cnt;            // [5 L + 1] phase counters
     uint8_t* dimg[2];         // digit images of GEMV inputs, by phase parity (layout of the shared digit area)
     float* ssp[2];            // per-128-row-tile sums of x^2 of the next RMSNorm input, by phase parity
@@ -347,8 +346,11 @@ struct RowWords {
     }
 };
 
+constexpr uint32_t kAttnMaxSplits = 8;
+
 template <int NV, int GQM, typename KVT>
-__device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint32_t tid, uint8_t* img) {
+__device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint32_t tid, uint8_t* img, uint32_t tag,
+                           bool& ok) {
     // GQM: query heads per KV head held in registers; B: keys per batch and warp
     constexpr int BW = 16 / RowWords<NV, KVT>::W;
     constexpr int B = BW > 8 ? 8 : (BW < 2 ? 2 : BW);
@@ -360,8 +362,8 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
     const KVT* kl = reinterpret_cast<const KVT*>(a.kc) + layer_off;
     const KVT* vl = reinterpret_cast<const KVT*>(a.vc) + layer_off;
     float* wm = reinterpret_cast<float*>(scratch);  // [9][GQ][HD + 2]
-    __shared__ uint32_t s_last;
     const uint32_t pstride = HD + 2;
+    const uint64_t tagw = (uint64_t)tag << 32;
     const uint32_t d0 = lane * NV;
     const bool active = d0 < HD;
     for (uint32_t it = blockIdx.x; it < a.KVH * S; it += G) {
@@ -436,8 +438,9 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
                 if (active) p[2 + d0 + i] = o[g][i];
         }
         digit_sync();
-        // CTA partial of this split
-        float* pg = a.att_part + (size_t)kvh * GQ * S * pstride;
+        // CTA partial of this split.  The CTA of split 0 keeps its own and merges the others (:148-184),
+        // which publish theirs as (tag, value) words and move on.
+        uint64_t* pg = a.att_part + (size_t)kvh * GQ * S * pstride;
         for (uint32_t e = tid; e < GQ * HD; e += kDigitThreads) {
             const uint32_t g = e / HD, d = e % HD;
             float M = -INFINITY;
@@ -454,37 +457,55 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
                     acc = fmaf(p[2 + d], f, acc);
                 }
             }
-            float* dst = pg + ((size_t)g * S + sidx) * pstride;
-            dst[2 + d] = acc;
-            if (d == 0) { dst[0] = M; dst[1] = lsum; }
-        }
-        __threadfence();
-        digit_sync();
-        if (tid == 0) s_last = atomicAdd(a.att_ticket + kvh, 1u) == S - 1 ? 1u : 0u;
-        digit_sync();
-        if (s_last) {
-            __threadfence();
-            for (uint32_t e = tid; e < GQ * HD; e += kDigitThreads) {
-                const uint32_t g = e / HD, d = e % HD;
-                const float* pb = pg + (size_t)g * S * pstride;
-                float M = -INFINITY;
-                for (uint32_t s = 0; s < S; ++s)
-                    if (__ldcg(pb + s * pstride + 1) > 0.0f) M = fmaxf(M, __ldcg(pb + s * pstride));
-                float lsum = 0.0f, acc = 0.0f;
-                for (uint32_t s = 0; s < S; ++s) {
-                    const float ll = __ldcg(pb + s * pstride + 1);
-                    if (ll > 0.0f) {
-                        const float f = expf(__ldcg(pb + s * pstride) - M);
-                        lsum = fmaf(ll, f, lsum);
-                        acc = fmaf(__ldcg(pb + s * pstride + 2 + d), f, acc);
+            if (sidx != 0) {
+                uint64_t* dst = pg + ((size_t)g * S + sidx) * pstride;
+                st_relaxed_u64(dst + 2 + d, tagw | __float_as_uint(acc));
+                if (d == 0) {
+                    st_relaxed_u64(dst, tagw | __float_as_uint(M));
+                    st_relaxed_u64(dst + 1, tagw | __float_as_uint(lsum));
+                }
+                continue;
+            }
+            // split 0: add the other splits' (m, l, o[d]) in split order (online rescaling), once all
+            // their tags are this phase's; a poll that finds one missing starts over
+            const bool own = lsum > 0.0f;
+            float ltot = own ? lsum : 0.0f, atot = own ? acc : 0.0f;
+            const uint64_t t0 = global_ns();
+            while (ok) {
+                bool have = true;
+                float Mr = own ? M : -INFINITY, lr = own ? lsum : 0.0f, ar = own ? acc : 0.0f;
+                for (uint32_t s = 1; s < S; ++s) {
+                    const uint64_t* src = pg + ((size_t)g * S + s) * pstride;
+                    const uint64_t wm_ = ld_relaxed_u64(src), wl = ld_relaxed_u64(src + 1), wo = ld_relaxed_u64(src + 2 + d);
+                    have = have && (uint32_t)(wm_ >> 32) == tag && (uint32_t)(wl >> 32) == tag && (uint32_t)(wo >> 32) == tag;
+                    const float ms = __uint_as_float((uint32_t)wm_), ls_ = __uint_as_float((uint32_t)wl);
+                    const float os = __uint_as_float((uint32_t)wo);
+                    if (!(ls_ > 0.0f)) continue;
+                    if (ms > Mr) {
+                        const float r = expf(Mr - ms);  // 0 while nothing is accumulated (Mr = -inf)
+                        lr = fmaf(lr, r, ls_);
+                        ar = fmaf(ar, r, os);
+                        Mr = ms;
+                    } else {
+                        const float f = expf(ms - Mr);
+                        lr = fmaf(ls_, f, lr);
+                        ar = fmaf(os, f, ar);
                     }
                 }
-                const float o = __fdiv_rn(acc, lsum);
-                a.attn[(size_t)(kvh * GQ + g) * HD + d] = o;
-                // digits of the o-proj input: this warp holds the 32 elements of one block
-                if (img) warp_block_digits(img, a.xstride, (kvh * GQ * HD + e) >> 5, o, lane);
+                if (have) {
+                    ltot = lr;
+                    atot = ar;
+                    break;
+                }
+                if (global_ns() - t0 > kWaitNs) {
+                    atomicExch(&a.st->error, 1u);
+                    ok = false;
+                }
             }
-            if (tid == 0) a.att_ticket[kvh] = 0;
+            const float o = __fdiv_rn(atot, ltot);
+            a.attn[(size_t)(kvh * GQ + g) * HD + d] = o;
+            // digits of the o-proj input: this warp holds the 32 elements of one block
+            if (img) warp_block_digits(img, a.xstride, (kvh * GQ * HD + e) >> 5, o, lane);
         }
         digit_sync();  // shared memory reused by the next item
     }
@@ -610,11 +631,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
         uint8_t* img_next = a.dimg[(p + 1) & 1];
         float* ssp_next = a.ssp[(p + 1) & 1];
         if (kind == kPhAttn) {
-            attn_phase<NV, GQM, KVT>(a, l, xb, tid, a.hd % 32 == 0 ? img_next : nullptr);
-            if (tid == 0) {
-                __threadfence();
-                red_add_release_gpu(a.cnt + p, 1u);
-            }
+            attn_phase<NV, GQM, KVT>(a, l, xb, tid, a.hd % 32 == 0 ? img_next : nullptr, ((launch + 1) << 10) | p, ok);
+            // the CTA's writes are ordered before the release by the barrier that ends the item
+            if (tid == 0) red_add_release_gpu(a.cnt + p, 1u);
             continue;
         }
         const Geo gm = phase_geo(mt, c, G);
