@@ -193,12 +193,18 @@ def run_ours(args):
     if args.layers:
         # truncated depth, for small profiler captures only (never a bench line)
         cfg.num_layers = args.layers
+    # N > 1: one sequence, tensor parallel over the N GPUs (--replicas: N independent sequences)
+    tpw = world if (world > 1 and not args.replicas) else 1
     t0 = time.time()
-    eng = bt.TransformerEngine(cfg, device=local, rope_theta=synthetic.ROPE_THETA[shape])
+    eng = bt.TransformerEngine(cfg, device=local, rope_theta=synthetic.ROPE_THETA[shape],
+                               tp_rank=rank if tpw > 1 else 0, tp_world=tpw)
     eng.generate(seed=0, sigma=0.02)
+    if tpw > 1:
+        from blocktensor_b200 import tp
+        tp.connect(eng)
     kv = bt.KVCache(eng, max_seq, bt.BT_KV_FP16)
     log(f"[ours] {shape}: weights generated on device in {time.time() - t0:.1f} s")
-    prompt = synthetic.tokens(rank, prompt_len, cfg.vocab_size)
+    prompt = synthetic.tokens(rank if tpw == 1 else 0, prompt_len, cfg.vocab_size)
     t0 = time.time()
     eng.begin(kv, prompt)
     eng.steps(kv, prompt_len)          # prompt, one position per step (untimed)
@@ -230,11 +236,15 @@ def run_ours(args):
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         ms = float(t.item())
     ms_step = ms / K
-    value = world * K / (ms / 1000.0)
+    seqs = world if tpw == 1 else 1  # sequences decoded side by side
+    value = seqs * K / (ms / 1000.0)
 
-    # algorithmic bytes per step, averaged over the timed contexts
+    # algorithmic bytes per step of this GPU (its share under tensor parallelism), over the timed contexts
     kvb = 2
-    bytes_avg = sum(synthetic.step_bytes(cfg, pos0 + i + 1, kvb) for i in range(K)) / K
+    if tpw == 1:
+        bytes_avg = sum(synthetic.step_bytes(cfg, pos0 + i + 1, kvb) for i in range(K)) / K
+    else:
+        bytes_avg = sum(kv.step_info(pos0 + i + 1)[1] for i in range(K)) / K
     peak, peak_kind = hbm_peak()
     achieved = bytes_avg / (ms_step / 1000.0) / 1e9
 
@@ -260,7 +270,12 @@ def run_ours(args):
         t = torch.tensor([e2e_s], device="cuda")
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = world * E / e2e_s
+    e2e = seqs * E / e2e_s
+    vocab_local = cfg.vocab_size
+    if tpw > 1:
+        from blocktensor_b200 import tp
+        vocab_local = tp.shard(cfg.vocab_size, cfg.dim, cfg.hidden_dim, cfg.num_heads, cfg.num_kv_heads,
+                               cfg.head_dim, rank, world).vocab  # this rank's logits come back
 
     # optional diagnostic: the same step as one launch per operation, events around every launch
     breakdown = None
@@ -271,7 +286,7 @@ def run_ours(args):
     # DRAM bytes per launch of the step kernel from an ncu capture (profiles/), scaled to this model
     traffic = None
     tfile = os.path.join(ROOT, "profiles", "decode_step_traffic.json")
-    if os.path.exists(tfile) and not args.layers:
+    if os.path.exists(tfile) and not args.layers and tpw == 1:
         try:
             traffic = json.load(open(tfile))[shape]["dram_bytes_per_launch"]
         except Exception:
@@ -291,12 +306,14 @@ def run_ours(args):
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int8", "data": "synthetic",
-            "config": {"workload": f"{shape}-shaped int8 decode, batch 1 per GPU", "model": shape,
-                       "global_batch": world, "seq_len": prompt_len, "prompt": prompt_len, "decode_steps": K,
-                       "kv_cache": "fp16", "activations": "fp32", "weights": "int8 Q8_0 (fp32 scale per 32)",
-                       "parallelism": f"replicas{world}" if world > 1 else "single",
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong" if tpw > 1 else "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": (f"{shape}-shaped int8 decode, batch 1, tensor parallel over {world} GPUs"
+                                    if tpw > 1 else f"{shape}-shaped int8 decode, batch 1 per GPU"),
+                       "model": shape, "global_batch": seqs, "seq_len": prompt_len, "prompt": prompt_len,
+                       "decode_steps": K, "kv_cache": "fp16", "activations": "fp32",
+                       "weights": "int8 Q8_0 (fp32 scale per 32)",
+                       "parallelism": f"tp{world}" if tpw > 1 else (f"replicas{world}" if world > 1 else "single"),
                        "l2": "inputs larger than L2 (7.4 GB of weights per step)",
                        "truncated_layers": args.layers or None},
             # the persistent step kernel is the only kernel of the timed region: one launch per token
@@ -306,7 +323,7 @@ def run_ours(args):
                          "us_per_launch": ms_step * 1000.0, "traffic": traffic,
                          "launch_per_op_breakdown_us": breakdown},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 32,
-                    "d2h_bytes_per_step": cfg.vocab_size * 4 + 32,
+                    "d2h_bytes_per_step": vocab_local * 4 + 32,
                     "api": "bt_engine_forward_token(host token, host logits)"},
             "gpu_launches": launches,
             "clocks": clk,
@@ -332,6 +349,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="also time the launch-per-operation step (per-kernel breakdown, diagnostic)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1: N independent sequences (one per GPU) instead of tensor parallelism")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0,
                     help="truncate the model to N layers (profiler captures; the JSON line is then marked)")

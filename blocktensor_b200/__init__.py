@@ -14,7 +14,7 @@ from typing import Sequence
 import numpy as np
 
 from . import native
-from .native import (BT_KV_FP16, BT_KV_FP32, CudaBackendError, EngineOptions, ModelConfig,
+from .native import (BT_KV_FP16, BT_KV_FP32, BT_TP_HANDLE_BYTES, CudaBackendError, EngineOptions, ModelConfig,
                      TensorView, call, load)
 
 __all__ = [
@@ -183,12 +183,16 @@ class TransformerEngine:
     signature and returns the logits as a numpy array.
     """
 
-    def __init__(self, config: ModelConfig, device: int = 0, rope_theta: float = 10000.0):
+    def __init__(self, config: ModelConfig, device: int = 0, rope_theta: float = 10000.0,
+                 tp_rank: int = 0, tp_world: int = 1):
         self.config = config
         self.device = device
         opt = EngineOptions()
         opt.rope_theta = rope_theta
+        opt.tp_rank = tp_rank
+        opt.tp_world = tp_world
         self.rope_theta = rope_theta
+        self.tp_rank, self.tp_world = tp_rank, tp_world
         h = C.c_void_p()
         call("bt_engine_create", device, C.byref(config), C.byref(opt), C.byref(h))
         self._h = h
@@ -258,6 +262,19 @@ class TransformerEngine:
         call("bt_engine_decode", self._h, kv.handle, p.ctypes.data, len(p), pos0, n_gen, out.ctypes.data)
         return out
 
+    def tp_handle(self) -> bytes:
+        """This rank's exchange handle (tensor parallelism; see tp.connect)."""
+        buf = C.create_string_buffer(BT_TP_HANDLE_BYTES)
+        call("bt_engine_tp_handle", self._h, buf)
+        return buf.raw
+
+    def tp_connect(self, handles: Sequence[bytes]):
+        """Maps every rank's exchange buffer; handles in rank order."""
+        if len(handles) != self.tp_world or any(len(h) != BT_TP_HANDLE_BYTES for h in handles):
+            raise ValueError("tp_connect: one handle of BT_TP_HANDLE_BYTES per rank")
+        buf = C.create_string_buffer(b"".join(handles), BT_TP_HANDLE_BYTES * self.tp_world)
+        call("bt_engine_tp_connect", self._h, buf)
+
     def set_taps(self, enable: bool = True):
         call("bt_engine_set_taps", self._h, int(enable))
 
@@ -326,6 +343,10 @@ class KVCache:
         pos, tok, am = C.c_uint32(), C.c_uint32(), C.c_uint32()
         call("bt_kv_state", self._h, C.byref(pos), C.byref(tok), C.byref(am))
         return pos.value, tok.value, am.value
+
+    def inject_stall(self):
+        """Test hook: the next step's device waits expire (bt_kv_inject_stall)."""
+        call("bt_kv_inject_stall", self._h)
 
     def step_info(self, context: int):
         launches, nbytes = C.c_uint64(), C.c_uint64()

@@ -21,6 +21,7 @@
 #include "bt_step.cuh"
 #include "bt_internal.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -44,7 +45,17 @@ struct LayerDev {
 
 struct bt_engine {
     int device = 0;
-    bt_model_config cfg{};
+    bt_model_config cfg{};  // the model
+    // this GPU's share of it (tensor parallelism over tp_world GPUs; the whole model when 1):
+    // heads, KV heads, FFN rows and head-matrix (vocab) rows of rank tp_rank, dim unchanged
+    bt_model_config lc{};
+    uint32_t tp_rank = 0, tp_world = 1;
+    uint32_t v0 = 0;  // first vocab row of this rank
+    uint64_t* tp_xbuf = nullptr;     // exchange buffer of this rank (own allocation, shared by IPC)
+    size_t tp_bytes = 0;
+    uint64_t** tp_peers = nullptr;   // [tp_world] every rank's exchange buffer as mapped here (device array)
+    std::vector<void*> tp_opened;    // peer buffers opened by IPC
+    bool tp_ready = false;
     float theta = 10000.0f;
     cudaStream_t stream = nullptr;
     bool pdl = true;
@@ -144,6 +155,7 @@ int dev_alloc(std::vector<void*>& list, T** out, size_t count, const char* what)
     } while (0)
 
 uint32_t kvd(const bt_model_config& c) { return c.num_kv_heads * c.head_dim; }
+uint32_t qd(const bt_model_config& c) { return c.num_heads * c.head_dim; }  // query rows (dim without TP)
 
 int validate_config(const bt_model_config& c) {
     if (c.vocab_size == 0 || c.dim == 0 || c.hidden_dim == 0 || c.num_layers == 0 || c.num_heads == 0 ||
@@ -167,22 +179,29 @@ int validate_config(const bt_model_config& c) {
 // Destination of each of the 9 per-layer tensors inside the fused device layout.
 struct Slot {
     uint8_t* units;
-    uint32_t rows, cols;
+    uint32_t rows, cols;  // of this rank's share
     RowMap map;
+    uint32_t grow0;       // its first row in the model's tensor
+    uint32_t gcols;       // columns of the model's tensor (its share: blocks cb0 .. cb0 + cols/32 - 1)
+    uint32_t cb0;
 };
 
+// Tensor parallelism: q/k/v, gate and up split by output rows (whole heads,
+// FFN rows), o and down by input columns (whole 32-blocks), so that o and
+// down give partial sums of x that the ranks add.
 Slot layer_slot(bt_engine* e, uint32_t l, int j) {
-    const auto& c = e->cfg;
+    const auto& c = e->lc;
     LayerDev& L = e->layers[l];
-    const uint32_t D = c.dim, F = c.hidden_dim, KV = kvd(c), hd = c.head_dim;
+    const uint32_t D = c.dim, F = c.hidden_dim, KV = kvd(c), Q = qd(c), hd = c.head_dim, r = e->tp_rank;
+    const uint32_t Fg = e->cfg.hidden_dim, Qg = qd(e->cfg);
     switch (j) {
-        case 2: return {L.qkv, D, D, RowMap{1, hd, 0, 0, 0}};
-        case 3: return {L.qkv, KV, D, RowMap{1, hd, 0, 0, D}};
-        case 4: return {L.qkv, KV, D, RowMap{0, 0, 0, 0, D + KV}};
-        case 5: return {L.o, D, D, RowMap{0, 0, 0, 0, 0}};
-        case 6: return {L.gu, F, D, RowMap{2, 0, 0, 0, 0}};
-        case 7: return {L.gu, F, D, RowMap{2, 0, 1, 0, 0}};
-        default: return {L.d, D, F, RowMap{0, 0, 0, 0, 0}};
+        case 2: return {L.qkv, Q, D, RowMap{1, hd, 0, 0, 0}, r * Q, D, 0};
+        case 3: return {L.qkv, KV, D, RowMap{1, hd, 0, 0, Q}, r * KV, D, 0};
+        case 4: return {L.qkv, KV, D, RowMap{0, 0, 0, 0, Q + KV}, r * KV, D, 0};
+        case 5: return {L.o, D, Q, RowMap{0, 0, 0, 0, 0}, 0, Qg, r * Q / 32};
+        case 6: return {L.gu, F, D, RowMap{2, 0, 0, 0, 0}, r * F, D, 0};
+        case 7: return {L.gu, F, D, RowMap{2, 0, 1, 0, 0}, r * F, D, 0};
+        default: return {L.d, D, F, RowMap{0, 0, 0, 0, 0}, 0, Fg, r * F / 32};
     }
 }
 
@@ -200,12 +219,13 @@ int alloc_units(bt_engine* e, uint8_t** out, uint32_t M, uint32_t K, const char*
 // whose query heads per KV head do not fit the kernel's registers use the
 // launch-per-kernel step.
 int plan_step(bt_engine* e) {
-    const auto& c = e->cfg;
+    const auto& c = e->lc;
     const uint32_t hd = c.head_dim, GQ = c.num_heads / c.num_kv_heads;
     e->step_nv = hd <= 64 ? 2 : hd <= 128 ? 4 : 8;
     // phases 5 L + 1 < 1024: the phase index is the low 10 bits of the split partials' tags
     e->step_ok = GQ * e->step_nv <= 16 && hd % e->step_nv == 0 && 5 * c.num_layers + 1 < 1024;
-    const uint32_t kmax = c.dim > c.hidden_dim ? c.dim : c.hidden_dim;
+    uint32_t kmax = c.dim > c.hidden_dim ? c.dim : c.hidden_dim;
+    if (qd(c) > kmax) kmax = qd(c);
     const size_t img_bytes = 2 * (size_t)mma_xstride(kmax) + ((kmax / 32) * 4 + 15) / 16 * 16;  // digits + block scales
     size_t scratch = img_bytes;
     const size_t attn = (size_t)kDigitWarps * GQ * (hd + 2) * 4;
@@ -225,11 +245,11 @@ int plan_step(bt_engine* e) {
     if (const char* v = std::getenv("BT_STEP_KERNEL")) e->use_step = (v[0] != '0');
     // the per-layer matrix table the kernel walks
     std::vector<StepLayer> tab(c.num_layers);
-    const uint32_t D = c.dim, F = c.hidden_dim, QKV = D + 2 * kvd(c);
+    const uint32_t D = c.dim, F = c.hidden_dim, Q = qd(c), QKV = Q + 2 * kvd(c);
     for (uint32_t l = 0; l < c.num_layers; ++l) {
         const LayerDev& L = e->layers[l];
         tab[l].qkv = StepMat{L.qkv, QKV, unit_rows(QKV), D};
-        tab[l].o = StepMat{L.o, D, unit_rows(D), D};
+        tab[l].o = StepMat{L.o, D, unit_rows(D), Q};
         tab[l].gu = StepMat{L.gu, 2 * F, unit_rows(2 * F), D};
         tab[l].d = StepMat{L.d, D, unit_rows(D), F};
         tab[l].attn_norm = L.attn_norm;
@@ -279,7 +299,9 @@ cudaError_t launch_step_t(const StepArgs& a, uint32_t grid, size_t smem, cudaStr
 
 // One decode step as one cooperative launch of the persistent kernel.
 int launch_step(bt_engine* e, bt_kv* kv, cudaStream_t s) {
-    const auto& c = e->cfg;
+    const auto& c = e->lc;
+    if (e->tp_world > 1 && !e->tp_ready)
+        return fail(BT_ERR_INVALID_ARGUMENT, "tensor parallel engine: bt_engine_tp_connect has not been called");
     StepArgs a{};
     a.layers = e->d_layers;
     a.head = StepMat{e->head, c.vocab_size, unit_rows(c.vocab_size), c.dim};
@@ -308,6 +330,11 @@ int launch_step(bt_engine* e, bt_kv* kv, cudaStream_t s) {
     }
     a.L = c.num_layers;
     a.D = c.dim;
+    a.DQ = qd(c);
+    a.v0 = e->v0;
+    a.tp_xch = e->tp_peers;
+    a.tp_rank = e->tp_rank;
+    a.tp_world = e->tp_world;
     a.F = c.hidden_dim;
     a.KVD = kvd(c);
     a.hd = c.head_dim;
@@ -344,26 +371,26 @@ int launch_step(bt_engine* e, bt_kv* kv, cudaStream_t s) {
 bool step_path(const bt_engine* e) { return e->use_step && e->step_ok; }
 
 int alloc_weights(bt_engine* e) {
-    const auto& c = e->cfg;
-    const size_t D = c.dim, F = c.hidden_dim, KV = kvd(c), V = c.vocab_size;
+    const auto& c = e->lc;
+    const size_t D = c.dim, F = c.hidden_dim, KV = kvd(c), V = c.vocab_size, Q = qd(c);
     auto& A = e->allocs;
-    BT_TRY_ALLOC(A, &e->embed, V * D, "embed");
+    BT_TRY_ALLOC(A, &e->embed, (size_t)e->cfg.vocab_size * D, "embed");  // every token's row on every rank
     BT_TRY_ALLOC(A, &e->out_norm, D, "out_norm");
     int rc = alloc_units(e, &e->head, (uint32_t)V, (uint32_t)D, "head");
     if (rc != BT_OK) return rc;
     e->layers.resize(c.num_layers);
     for (uint32_t l = 0; l < c.num_layers; ++l) {
         LayerDev& L = e->layers[l];
-        if ((rc = alloc_units(e, &L.qkv, (uint32_t)(D + 2 * KV), (uint32_t)D, "wqkv"))) return rc;
-        if ((rc = alloc_units(e, &L.o, (uint32_t)D, (uint32_t)D, "wo"))) return rc;
+        if ((rc = alloc_units(e, &L.qkv, (uint32_t)(Q + 2 * KV), (uint32_t)D, "wqkv"))) return rc;
+        if ((rc = alloc_units(e, &L.o, (uint32_t)D, (uint32_t)Q, "wo"))) return rc;
         if ((rc = alloc_units(e, &L.gu, (uint32_t)(2 * F), (uint32_t)D, "wgu"))) return rc;
         if ((rc = alloc_units(e, &L.d, (uint32_t)D, (uint32_t)F, "wd"))) return rc;
         BT_TRY_ALLOC(A, &L.attn_norm, D, "attn_norm");
         BT_TRY_ALLOC(A, &L.ffn_norm, D, "ffn_norm");
     }
     BT_TRY_ALLOC(A, &e->x, D, "x");
-    BT_TRY_ALLOC(A, &e->q, D, "q");
-    BT_TRY_ALLOC(A, &e->attn, D, "attn");
+    BT_TRY_ALLOC(A, &e->q, Q, "q");
+    BT_TRY_ALLOC(A, &e->attn, Q, "attn");
     BT_TRY_ALLOC(A, &e->act, F, "act");
     BT_TRY_ALLOC(A, &e->logits, V, "logits");
     BT_TRY_ALLOC(A, &e->taps, (size_t)c.num_layers * D, "taps");
@@ -375,7 +402,8 @@ int alloc_weights(bt_engine* e) {
     // split scratch of the GEMVs: partials [SM][2][128], one ticket per row tile of the tallest matrix
     uint32_t rows = (uint32_t)V;
     if (2 * F > rows) rows = (uint32_t)(2 * F);
-    if (D + 2 * KV > rows) rows = (uint32_t)(D + 2 * KV);
+    if (Q + 2 * KV > rows) rows = (uint32_t)(Q + 2 * KV);
+    if (D > rows) rows = (uint32_t)D;
     const size_t tickets = mma_row_tiles(unit_rows(rows));
     // floats for the standalone GEMVs; (tag, value) words for the step kernel, zeroed (tag 0 is never valid)
     BT_TRY_ALLOC(A, &e->split_part, (size_t)e->num_sms * 2 * kTileRows * 2, "split partials");
@@ -571,7 +599,29 @@ int bt_engine_create(int device, const bt_model_config* cfg, const bt_engine_opt
     auto e = std::make_unique<bt_engine>();
     e->device = device;
     e->cfg = *cfg;
+    e->lc = *cfg;
     if (opt && opt->rope_theta > 0.0f) e->theta = opt->rope_theta;
+    if (opt && opt->tp_world > 1) {
+        // tensor parallelism: rank tp_rank of tp_world takes whole heads, KV heads and 32-blocks of FFN
+        // rows (o and down are split by these as input columns), and a contiguous slice of the vocab
+        const uint32_t W = opt->tp_world, r = opt->tp_rank;
+        if (W > kTpMaxWorld || r >= W)
+            return fail(BT_ERR_INVALID_ARGUMENT, "bt_engine_create: tp_rank must be < tp_world <= 8");
+        if (cfg->num_kv_heads % W || cfg->num_heads % W || (cfg->num_heads / W * cfg->head_dim) % 32 ||
+            cfg->hidden_dim % (32 * W))
+            return fail(BT_ERR_INVALID_ARGUMENT,
+                        "bt_engine_create: tp_world must divide the KV heads, and each rank's query rows and FFN rows "
+                        "must be whole 32-blocks");
+        e->tp_rank = r;
+        e->tp_world = W;
+        e->lc.num_heads = cfg->num_heads / W;
+        e->lc.num_kv_heads = cfg->num_kv_heads / W;
+        e->lc.hidden_dim = cfg->hidden_dim / W;
+        const uint32_t vl = (cfg->vocab_size + W - 1) / W;
+        e->v0 = r * vl;
+        e->lc.vocab_size = e->v0 < cfg->vocab_size ? std::min(vl, cfg->vocab_size - e->v0) : 0;
+        if (e->lc.vocab_size == 0) return fail(BT_ERR_INVALID_ARGUMENT, "bt_engine_create: tp_world above the vocab");
+    }
     if (const char* v = std::getenv("BT_NO_PDL")) e->pdl = (v[0] == '0');
     if (const char* v = std::getenv("BT_NO_GRAPH")) e->use_graph = (v[0] == '0');
     if (const char* v = std::getenv("BT_GEMV_PREFETCH_KB")) {
@@ -583,6 +633,17 @@ int bt_engine_create(int device, const bt_model_config* cfg, const bt_engine_opt
     e->num_sms = nsm > 0 ? (uint32_t)nsm : 148;
     BT_CUDA_CHECK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     rc = alloc_weights(e.get());
+    if (rc == BT_OK && e->tp_world > 1) {
+        if (!step_path(e.get()))
+            rc = fail(BT_ERR_INVALID_ARGUMENT, "bt_engine_create: tensor parallelism needs the persistent step kernel");
+        // exchange buffer: o-proj and down partials [2][tp_world][dim], then [tp_world][2] argmax words
+        e->tp_bytes = sizeof(uint64_t) * (2 * (size_t)e->tp_world * cfg->dim + 2 * e->tp_world);
+        cudaError_t ce = cudaSuccess;
+        if (rc == BT_OK) ce = cudaMalloc(&e->tp_xbuf, e->tp_bytes);
+        if (rc == BT_OK && ce == cudaSuccess) ce = cudaMemset(e->tp_xbuf, 0, e->tp_bytes);  // tag 0: never valid
+        if (rc == BT_OK && ce == cudaSuccess) ce = cudaMalloc(&e->tp_peers, sizeof(uint64_t*) * e->tp_world);
+        if (rc == BT_OK && ce != cudaSuccess) rc = fail(BT_ERR_CUDA, cudaGetErrorString(ce));
+    }
     if (rc != BT_OK) {
         std::string msg = bt_cuda_last_error();
         bt_engine_destroy(e.release());
@@ -590,6 +651,46 @@ int bt_engine_create(int device, const bt_model_config* cfg, const bt_engine_opt
         return rc;
     }
     *out = e.release();
+    return BT_OK;
+}
+
+int bt_engine_tp_handle(bt_engine* e, void* handle) {
+    if (!e || !handle) return fail(BT_ERR_INVALID_ARGUMENT, "bt_engine_tp_handle: null argument");
+    if (e->tp_world < 2) return fail(BT_ERR_INVALID_ARGUMENT, "bt_engine_tp_handle: not a tensor parallel engine");
+    DeviceGuard guard(e->device);
+    cudaIpcMemHandle_t h;
+    BT_CUDA_CHECK(cudaIpcGetMemHandle(&h, e->tp_xbuf));
+    static_assert(sizeof(h) == BT_TP_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle, &h, sizeof(h));
+    return BT_OK;
+}
+
+int bt_engine_tp_connect(bt_engine* e, const void* handles) {
+    if (!e || !handles) return fail(BT_ERR_INVALID_ARGUMENT, "bt_engine_tp_connect: null argument");
+    if (e->tp_world < 2) return fail(BT_ERR_INVALID_ARGUMENT, "bt_engine_tp_connect: not a tensor parallel engine");
+    if (e->tp_ready) return fail(BT_ERR_INVALID_ARGUMENT, "bt_engine_tp_connect: already connected");
+    DeviceGuard guard(e->device);
+    std::vector<uint64_t*> ptrs(e->tp_world, nullptr);
+    for (uint32_t q = 0; q < e->tp_world; ++q) {
+        if (q == e->tp_rank) {
+            ptrs[q] = e->tp_xbuf;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)q * BT_TP_HANDLE_BYTES, sizeof(h));
+        void* p = nullptr;
+        const cudaError_t ce = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (ce != cudaSuccess) {
+            for (void* o : e->tp_opened) cudaIpcCloseMemHandle(o);
+            e->tp_opened.clear();
+            return fail(BT_ERR_CUDA, std::string("bt_engine_tp_connect: rank ") + std::to_string(q) + ": " +
+                                         cudaGetErrorString(ce));
+        }
+        e->tp_opened.push_back(p);
+        ptrs[q] = static_cast<uint64_t*>(p);
+    }
+    BT_CUDA_CHECK(cudaMemcpy(e->tp_peers, ptrs.data(), sizeof(uint64_t*) * e->tp_world, cudaMemcpyHostToDevice));
+    e->tp_ready = true;
     return BT_OK;
 }
 
@@ -604,6 +705,9 @@ int bt_engine_destroy(bt_engine* e) {
         kv->e = nullptr;
     }
     e->kvs.clear();
+    for (void* p : e->tp_opened) cudaIpcCloseMemHandle(p);
+    if (e->tp_peers) cudaFree(e->tp_peers);
+    if (e->tp_xbuf) cudaFree(e->tp_xbuf);
     for (void* p : e->allocs) cudaFree(p);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
@@ -645,27 +749,26 @@ int bt_engine_load(bt_engine* e, const bt_tensor_view* t, uint32_t n, int on_dev
     for (size_t b : {qbytes(F, D), qbytes(D, F)}) max_q = b > max_q ? b : max_q;
     void* stage = nullptr;
     if (!on_device) BT_CUDA_CHECK(cudaMalloc(&stage, max_q));
-    auto load_q = [&](const bt_tensor_view& tv, uint8_t* units, uint32_t rows, uint32_t cols, RowMap m) -> int {
-        const void* src = tv.data;
+    // this rank's rows (and, for o and down, its columns) of a tensor
+    auto load_q = [&](const bt_tensor_view& tv, const Slot& sl) -> int {
+        const size_t row_bytes = (size_t)sl.gcols / 32 * 36;
+        const void* src = static_cast<const uint8_t*>(tv.data) + (size_t)sl.grow0 * row_bytes;
         if (!on_device) {
-            BT_CUDA_CHECK(cudaMemcpyAsync(stage, tv.data, tv.bytes, cudaMemcpyHostToDevice, s));
+            BT_CUDA_CHECK(cudaMemcpyAsync(stage, src, (size_t)sl.rows * row_bytes, cudaMemcpyHostToDevice, s));
             src = stage;
         }
-        BT_CUDA_CHECK(launch_pack_units(src, units, rows, cols, m, s));
+        BT_CUDA_CHECK(launch_pack_units(src, sl.units, sl.rows, sl.cols, sl.map, s, sl.gcols / 32, sl.cb0));
         if (!on_device) BT_CUDA_CHECK(cudaStreamSynchronize(s));  // stage is reused
         return BT_OK;
     };
-    rc = load_q(t[2], e->head, c.vocab_size, c.dim, RowMap{0, 0, 0, 0, 0});
+    rc = load_q(t[2], Slot{e->head, e->lc.vocab_size, c.dim, RowMap{0, 0, 0, 0, 0}, e->v0, c.dim, 0});
     for (uint32_t l = 0; rc == BT_OK && l < c.num_layers; ++l) {
         LayerDev& L = e->layers[l];
         const bt_tensor_view* tl = t + 3 + 9 * l;
         cudaError_t ce = cudaMemcpyAsync(L.attn_norm, tl[0].data, tl[0].bytes, kind, s);
         if (ce == cudaSuccess) ce = cudaMemcpyAsync(L.ffn_norm, tl[1].data, tl[1].bytes, kind, s);
         if (ce != cudaSuccess) { rc = fail(BT_ERR_CUDA, cudaGetErrorString(ce)); break; }
-        for (int j = 2; j < 9 && rc == BT_OK; ++j) {
-            Slot sl = layer_slot(e, l, j);
-            rc = load_q(tl[j], sl.units, sl.rows, sl.cols, sl.map);
-        }
+        for (int j = 2; j < 9 && rc == BT_OK; ++j) rc = load_q(tl[j], layer_slot(e, l, j));
     }
     cudaError_t ce = cudaStreamSynchronize(s);
     if (stage) cudaFree(stage);
@@ -693,31 +796,30 @@ int bt_engine_generate(bt_engine* e, uint64_t seed, float sigma) {
         return fail(BT_ERR_OUT_OF_MEMORY, "bt_engine_generate: staging allocation failed");
     }
     int rc = BT_OK;
-    auto gen_q = [&](uint32_t stream_id, uint8_t* units, size_t rows, size_t cols, RowMap m) -> int {
-        const size_t rows_per = slab / cols;
+    // this rank's rows of the model's tensor (whole rows generated, its columns packed)
+    auto gen_q = [&](uint32_t stream_id, const Slot& sl) -> int {
+        const size_t gcols = sl.gcols, rows = sl.rows;
+        const size_t rows_per = slab / gcols;
         for (size_t r0 = 0; r0 < rows; r0 += rows_per) {
             const size_t nr = (rows - r0) < rows_per ? (rows - r0) : rows_per;
-            BT_CUDA_CHECK(launch_gen_normal(seed, stream_id, r0 * cols, nr * cols, k, tmp, s));
-            BT_CUDA_CHECK(launch_quantize_q8_0(tmp, blk, nr * cols / 32, s));
-            RowMap mm = m;
+            BT_CUDA_CHECK(launch_gen_normal(seed, stream_id, (sl.grow0 + r0) * gcols, nr * gcols, k, tmp, s));
+            BT_CUDA_CHECK(launch_quantize_q8_0(tmp, blk, nr * gcols / 32, s));
+            RowMap mm = sl.map;
             mm.src_off = (uint32_t)r0;
-            BT_CUDA_CHECK(launch_pack_units(blk, units, (uint32_t)nr, (uint32_t)cols, mm, s));
+            BT_CUDA_CHECK(launch_pack_units(blk, sl.units, (uint32_t)nr, sl.cols, mm, s, (uint32_t)(gcols / 32), sl.cb0));
         }
         return BT_OK;
     };
     ce = launch_gen_normal(seed, 0, 0, V * D, k, e->embed, s);
     if (ce == cudaSuccess) ce = launch_fill(e->out_norm, D, 1.0f, s);
     if (ce != cudaSuccess) rc = fail(BT_ERR_CUDA, cudaGetErrorString(ce));
-    if (rc == BT_OK) rc = gen_q(2, e->head, V, D, RowMap{0, 0, 0, 0, 0});
+    if (rc == BT_OK) rc = gen_q(2, Slot{e->head, e->lc.vocab_size, (uint32_t)D, RowMap{0, 0, 0, 0, 0}, e->v0, (uint32_t)D, 0});
     for (uint32_t l = 0; rc == BT_OK && l < c.num_layers; ++l) {
         LayerDev& L = e->layers[l];
         ce = launch_fill(L.attn_norm, D, 1.0f, s);
         if (ce == cudaSuccess) ce = launch_fill(L.ffn_norm, D, 1.0f, s);
         if (ce != cudaSuccess) { rc = fail(BT_ERR_CUDA, cudaGetErrorString(ce)); break; }
-        for (int j = 2; j < 9 && rc == BT_OK; ++j) {
-            Slot sl = layer_slot(e, l, j);
-            rc = gen_q(16 + 16 * l + j, sl.units, sl.rows, sl.cols, sl.map);
-        }
+        for (int j = 2; j < 9 && rc == BT_OK; ++j) rc = gen_q(16 + 16 * l + j, layer_slot(e, l, j));
     }
     (void)KV; (void)F;
     ce = cudaStreamSynchronize(s);
@@ -735,7 +837,7 @@ int bt_kv_create(bt_engine* e, uint32_t max_seq, int dtype, bt_kv** out) {
     if (dtype != BT_KV_FP32 && dtype != BT_KV_FP16) return fail(BT_ERR_INVALID_ARGUMENT, "bt_kv_create: bad kv dtype");
     *out = nullptr;
     DeviceGuard guard(e->device);
-    const auto& c = e->cfg;
+    const auto& c = e->lc;
     auto kv = std::make_unique<bt_kv>();
     kv->e = e;
     kv->max_seq = max_seq;
@@ -828,7 +930,7 @@ int bt_kv_read_layer(bt_kv* kv, uint32_t layer, float* k, float* v) {
     if (!kv || !k || !v) return fail(BT_ERR_INVALID_ARGUMENT, "bt_kv_read_layer: null argument");
     if (!kv->e) return fail(BT_ERR_INVALID_ARGUMENT, "KV cache outlived its engine");
     bt_engine* e = kv->e;
-    const auto& c = e->cfg;
+    const auto& c = e->lc;  // this rank's KV heads
     if (layer >= c.num_layers) return fail(BT_ERR_OUT_OF_RANGE, "KVCache layer out of bounds");
     DeviceGuard guard(e->device);
     const size_t per = (size_t)c.num_kv_heads * kv->max_seq * c.head_dim;
@@ -873,7 +975,8 @@ int bt_engine_forward_token(bt_engine* e, bt_kv* kv, uint32_t token, uint32_t po
     rc = run_steps(e, kv, 1, s);
     if (rc != BT_OK) return rc;
     if (logits)
-        BT_CUDA_CHECK(cudaMemcpyAsync(logits, e->logits, sizeof(float) * e->cfg.vocab_size, cudaMemcpyDeviceToHost, s));
+        BT_CUDA_CHECK(cudaMemcpyAsync(logits + e->v0, e->logits, sizeof(float) * e->lc.vocab_size,
+                                      cudaMemcpyDeviceToHost, s));  // this rank's vocab rows
     BT_CUDA_CHECK(cudaMemcpyAsync(h, kv->st, sizeof(DevState), cudaMemcpyDeviceToHost, s));
     BT_CUDA_CHECK(cudaStreamSynchronize(s));
     if (h->error) return fail(BT_ERR_DEVICE_TIMEOUT, "device wait timed out during the decode step");
@@ -947,9 +1050,9 @@ int bt_engine_read_taps(bt_engine* e, float* taps) {
 int bt_kv_step_info(bt_kv* kv, uint32_t context, uint64_t* launches, uint64_t* bytes) {
     if (!kv) return fail(BT_ERR_INVALID_ARGUMENT, "null KV cache");
     if (!kv->e) return fail(BT_ERR_INVALID_ARGUMENT, "KV cache outlived its engine");
-    const auto& c = kv->e->cfg;
-    const uint64_t D = c.dim, F = c.hidden_dim, KV = kvd(c), V = c.vocab_size, L = c.num_layers;
-    const uint64_t params = L * (D * D * 2 + KV * D * 2 + F * D * 3) + V * D;
+    const auto& c = kv->e->lc;  // this rank's share
+    const uint64_t D = c.dim, F = c.hidden_dim, KV = kvd(c), V = c.vocab_size, L = c.num_layers, Q = qd(c);
+    const uint64_t params = L * (Q * D * 2 + KV * D * 2 + F * D * 3) + V * D;
     const uint64_t weight_bytes = params + params / 32 * 4;
     const uint64_t norms = 4 * D * (2 * L + 1);
     const uint64_t emb = 4 * D;
@@ -970,6 +1073,21 @@ int bt_kv_state(bt_kv* kv, uint32_t* pos, uint32_t* token, uint32_t* last_argmax
     if (pos) *pos = h.pos;
     if (token) *token = h.cur_token;
     if (last_argmax) *last_argmax = h.last_argmax;
+    if (h.error) return fail(BT_ERR_DEVICE_TIMEOUT, "device wait timed out during an earlier step");
+    return BT_OK;
+}
+
+int bt_kv_inject_stall(bt_kv* kv) {
+    if (!kv) return fail(BT_ERR_INVALID_ARGUMENT, "null KV cache");
+    bt_engine* e = kv->e;
+    if (!e) return fail(BT_ERR_INVALID_ARGUMENT, "KV cache outlived its engine");
+    if (!step_path(e)) return fail(BT_ERR_INVALID_ARGUMENT, "inject_stall: the engine does not run the step kernel");
+    DeviceGuard guard(e->device);
+    // the step count 2^20: a phase's CTAs wait for G (2^20 + 1) arrivals while only G can come
+    // (the signed difference stays negative for any grid below 2048 CTAs)
+    const uint32_t far = 1u << 20;
+    BT_CUDA_CHECK(cudaStreamSynchronize(e->stream));
+    BT_CUDA_CHECK(cudaMemcpy(&kv->st->pad[0], &far, sizeof(far), cudaMemcpyHostToDevice));
     return BT_OK;
 }
 

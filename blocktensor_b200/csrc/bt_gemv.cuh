@@ -205,6 +205,12 @@ struct EpiLogits {
     // persistent step kernel: the last CTA also counts the step in st->pad[0] and
     // the engine's step launches in ticket[1] (the tag of its split partials)
     bool bump_epoch = false;
+    // tensor parallelism: this rank's vocab rows start at v0; with tp_world > 1 the last CTA trades
+    // its best (value, index) with the other ranks through the argmax slots of their exchange
+    // buffers (xch[q] + xch_off: [tp_world][2] tagged words) and every rank takes the same token
+    uint32_t v0 = 0, tp_rank = 0, tp_world = 1, tag = 0;
+    uint64_t* const* xch = nullptr;
+    size_t xch_off = 0;
     template <int ROWS>
     __device__ void finish(const float* yr, uint32_t row0, uint32_t M) const {
         __shared__ bool s_last;

@@ -362,6 +362,37 @@ struct SEpiLogits {
         }
         warp_argmax(bv, bi);
         if (lane == 0) {
+            if (bi != 0xFFFFFFFFu) bi += e.v0;  // vocab index
+            if (e.tp_world > 1) {
+                // every rank's best to every rank, then the best of all in rank (= vocab) order
+                const uint64_t tagw = (uint64_t)e.tag << 32;
+                for (uint32_t q = 0; q < e.tp_world; ++q) {
+                    uint64_t* slot = e.xch[q] + e.xch_off + 2 * e.tp_rank;
+                    st_relaxed_sys_u64(slot, tagw | __float_as_uint(bv));
+                    st_relaxed_sys_u64(slot + 1, tagw | bi);
+                }
+                const uint64_t* own = e.xch[e.tp_rank] + e.xch_off;
+                float gv = -INFINITY;
+                uint32_t gi = 0xFFFFFFFFu;
+                const uint64_t t0 = global_ns();
+                for (uint32_t q = 0; q < e.tp_world; ++q) {
+                    uint64_t wv = 0, wi = 0;
+                    while (true) {
+                        wv = ld_relaxed_sys_u64(own + 2 * q);
+                        wi = ld_relaxed_sys_u64(own + 2 * q + 1);
+                        if ((uint32_t)(wv >> 32) == e.tag && (uint32_t)(wi >> 32) == e.tag) break;
+                        if (global_ns() - t0 > kWaitNs) {
+                            atomicExch(&e.st->error, 1u);
+                            break;
+                        }
+                    }
+                    const float v = __uint_as_float((uint32_t)wv);
+                    const uint32_t ix = (uint32_t)wi;
+                    if (ix != 0xFFFFFFFFu && (gi == 0xFFFFFFFFu || better(v, ix, gv, gi))) { gv = v; gi = ix; }
+                }
+                bv = gv;
+                bi = gi;
+            }
             const uint32_t ix = bi == 0xFFFFFFFFu ? 0 : bi;
             DevState* st = e.st;
             const uint32_t pos = st->pos;

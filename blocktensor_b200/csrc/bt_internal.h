@@ -21,8 +21,9 @@ cudaError_t launch_dequantize_q8_0(const void* src, float* dst, uint64_t n, cuda
 cudaError_t launch_repack_q8_0(const void* blocks, int8_t* qs, float* scales, uint32_t M, uint32_t K,
                                RowMap map, cudaStream_t s);
 // 36-byte blocks -> 576-byte mma units (rows padded to 16; the caller zeroes padding).
+// src_bpr: blocks per source row (0: K/32); cb0: first packed block of each source row.
 cudaError_t launch_pack_units(const void* blocks, uint8_t* units, uint32_t M, uint32_t K, RowMap map,
-                              cudaStream_t s);
+                              cudaStream_t s, uint32_t src_bpr = 0, uint32_t cb0 = 0);
 inline uint64_t unit_bytes(uint32_t M, uint32_t K) { return (uint64_t)((M + 127) / 128) * (K / 32) * 4608; }
 cudaError_t launch_gen_normal(uint64_t seed, uint64_t stream_id, uint64_t offset, uint64_t n, float k,
                               float* out, cudaStream_t s);

@@ -1,6 +1,8 @@
 // bt_ptx.cuh -- thin wrappers over the PTX the kernels need: mbarriers,
 // 1-D bulk (TMA) copies, named barriers, %globaltimer, and tcgen05 (tensor
-// memory, int8 MMA).  No multicast form of any copy is used anywhere.
+// memory, int8 MMA).  Every bulk copy reads this GPU's own memory into the
+// issuing CTA's shared memory; other GPUs' memory is reached only by plain
+// loads and stores (tensor parallel exchange).
 #pragma once
 
 #include "bt_common.cuh"
@@ -191,6 +193,17 @@ __device__ __forceinline__ void st_relaxed_u64(uint64_t* p, uint64_t v) {
 __device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
     uint64_t v;
     asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// The same across GPUs (peer memory mapped over NVLink): system scope.
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 

@@ -98,15 +98,17 @@ __global__ void repack_q8_0_kernel(const uint8_t* __restrict__ blocks, int8_t* _
 // dr/128, row rl = dr%128 of tile (dr/128, b); its 32 int8 go to the UMMA
 // K-major canonical layout (bytes 0-15 to offset (rl/8)*256 + (rl%8)*16, bytes
 // 16-31 to that + 128) and its scale to float rl after the 4096 weight bytes.
-// Padding rows stay zero.
+// Padding rows stay zero.  The source rows hold src_bpr blocks, of which
+// blocks cb0 .. cb0 + K/32 - 1 are packed (a column slice, for tensor
+// parallelism; src_bpr = K/32 and cb0 = 0 pack whole rows).
 __global__ void pack_units_kernel(const uint8_t* __restrict__ blocks, uint8_t* __restrict__ units, uint32_t M,
-                                  uint32_t K, RowMap map) {
+                                  uint32_t K, RowMap map, uint32_t src_bpr, uint32_t cb0) {
     const uint64_t nb = (uint64_t)M * (K / 32);
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= nb) return;
     const uint32_t bpr = K / 32;
     const uint32_t r = (uint32_t)(i / bpr), b = (uint32_t)(i % bpr);
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(blocks + i * 36);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(blocks + ((uint64_t)r * src_bpr + cb0 + b) * 36);
     const uint32_t dr = map_row(r, map);
     const uint32_t rl = dr % 128;
     uint8_t* tile = units + ((uint64_t)(dr / 128) * bpr + b) * 4608;
@@ -185,11 +187,13 @@ cudaError_t launch_repack_q8_0(const void* blocks, int8_t* qs, float* scales, ui
 }
 
 cudaError_t launch_pack_units(const void* blocks, uint8_t* units, uint32_t M, uint32_t K, RowMap map,
-                              cudaStream_t s) {
+                              cudaStream_t s, uint32_t src_bpr, uint32_t cb0) {
     const uint64_t nb = (uint64_t)M * (K / 32);
     if (nb == 0) return cudaSuccess;
+    if (src_bpr == 0) src_bpr = K / 32;
     g_launches.fetch_add(1, std::memory_order_relaxed);
-    pack_units_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, s>>>((const uint8_t*)blocks, units, M, K, map);
+    pack_units_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, s>>>((const uint8_t*)blocks, units, M, K, map,
+                                                                     src_bpr, cb0);
     return cudaGetLastError();
 }
 

@@ -65,9 +65,17 @@ struct StepArgs {
     uint8_t* dimg[2];         // digit images of GEMV inputs, by phase parity (layout of the shared digit area)
     float* ssp[2];            // per-128-row-tile sums of x^2 of the next RMSNorm input, by phase parity
     uint32_t L, D, KVD, F, hd, KVH, GQ, max_seq, S_att;
+    uint32_t DQ;              // query rows (heads of this rank x hd; D without tensor parallelism)
+    uint32_t v0;              // first vocab row of this rank's head matrix
+    // tensor parallelism over tp_world GPUs (1: none): every rank's exchange buffer, mapped here;
+    // [0] o-proj and [1] down partials, [tp_world][D] tagged words each, then the argmax slots
+    uint64_t* const* tp_xch;
+    uint32_t tp_rank, tp_world;
     float eps, scale;
     uint32_t NS, xstride, tmem_cols, scratch_off;
 };
+
+constexpr uint32_t kTpMaxWorld = 8;  // GPUs of one tensor parallel group
 
 enum : uint32_t { kPhQKV = 0, kPhAttn = 1, kPhO = 2, kPhGU = 3, kPhDown = 4, kPhHead = 5 };
 
@@ -612,7 +620,6 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
     const uint32_t target = G * (epoch + 1);
     const uint32_t pos = a.st->pos;  // changed only by the head phase's last CTA, at the very end
     const uint32_t launch = a.am_ticket[1];  // step launches of the engine so far (bumped at the very end)
-    const uint32_t Dtiles = (a.D + kTileRows - 1) / kTileRows;
     bool ok = true;
     // per-role pipeline state, carried across phases
     uint32_t rs = 0, rph = 0;              // ring slot (issuers, accumulators)
@@ -720,8 +727,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
 #pragma unroll
                     for (int i = 0; i < 2; ++i) {
                         const uint32_t r = row0 + 2 * (lane + 32 * i);
-                        const uint32_t local = r < a.D ? r : r - a.D;
-                        cs[i] = (r < a.D + a.KVD && pos < a.max_seq) ? a.rope[(size_t)pos * half + ((local % a.hd) >> 1)]
+                        const uint32_t local = r < a.DQ ? r : r - a.DQ;
+                        cs[i] = (r < a.DQ + a.KVD && pos < a.max_seq) ? a.rope[(size_t)pos * half + ((local % a.hd) >> 1)]
                                                                      : make_float2(1.0f, 0.0f);
                     }
                 }
@@ -777,6 +784,50 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                         }
                     }
                 }
+                if (resid && a.tp_world > 1 && ok) {
+                    // tensor parallelism: y is this rank's partial over its input columns.  Send it to
+                    // every rank, then add all ranks' partials in rank order (the same sum on every rank,
+                    // so the replicated x stays identical)
+                    const uint32_t W = a.tp_world, region = kind == kPhO ? 0 : 1;
+                    const uint64_t tagw = (uint64_t)tag << 32;
+                    for (uint32_t q = 0; q < W; ++q) {
+                        uint64_t* dst = a.tp_xch[q] + ((size_t)region * W + a.tp_rank) * a.D + row0;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            if (row0 + lane + 32 * i < mt.M) st_relaxed_sys_u64(dst + lane + 32 * i, tagw | __float_as_uint(v[i]));
+                    }
+                    const uint64_t* own = a.tp_xch[a.tp_rank] + (size_t)region * W * a.D + row0;
+                    float y[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    const uint64_t t0 = global_ns();
+                    for (uint32_t qb = 0; qb < W && ok;) {
+                        // 4 ranks' words in flight; a poll that finds one missing reads the group again
+                        float ys[4] = {y[0], y[1], y[2], y[3]};
+                        bool have = true;
+#pragma unroll
+                        for (uint32_t u = 0; u < 4; ++u) {
+                            const uint32_t q = qb + u;
+                            if (q >= W) break;
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const uint32_t r = row0 + lane + 32 * i;
+                                if (r >= mt.M) continue;
+                                const uint64_t w = ld_relaxed_sys_u64(own + (size_t)q * a.D + lane + 32 * i);
+                                have = have && (uint32_t)(w >> 32) == tag;
+                                ys[i] += __uint_as_float((uint32_t)w);
+                            }
+                        }
+                        if (__all_sync(0xffffffffu, have)) {
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) y[i] = ys[i];
+                            qb += 4;
+                        } else if (global_ns() - t0 > kWaitNs) {
+                            if (lane == 0) atomicExch(err, 1u);
+                            ok = false;
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) v[i] = y[i];
+                }
                 if (resid) {
                     // x += y (transformer_engine.cpp:191-195, 222-225), optional per-layer tap, then the
                     // next phase's digits of x * w_next and this tile's sum of x^2
@@ -824,9 +875,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                             const uint32_t r = row0 + 2 * pp;
                             if (r >= mt.M) continue;
                             const float x0 = fin[2 * pp], x1 = fin[2 * pp + 1];
-                            if (r < a.D + a.KVD) {
-                                const bool isq = r < a.D;
-                                const uint32_t local = isq ? r : r - a.D;
+                            if (r < a.DQ + a.KVD) {
+                                const bool isq = r < a.DQ;
+                                const uint32_t local = isq ? r : r - a.DQ;
                                 const uint32_t h = local / a.hd, j = (local % a.hd) >> 1;
                                 const float o1 = __fsub_rn(__fmul_rn(x0, cs[i].x), __fmul_rn(x1, cs[i].y));
                                 const float o2 = __fadd_rn(__fmul_rn(x0, cs[i].y), __fmul_rn(x1, cs[i].x));
@@ -839,7 +890,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                                     dst[j + half] = KVConv<KVT>::from_f(o2);
                                 }
                             } else {
-                                const uint32_t local = r - a.D - a.KVD;
+                                const uint32_t local = r - a.DQ - a.KVD;
                                 const uint32_t h = local / a.hd, d = local % a.hd;
                                 KVT* dst = vl + ((size_t)h * a.max_seq + pos) * a.hd;
                                 dst[d] = KVConv<KVT>::from_f(x0);
@@ -858,6 +909,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
             }
             if (kind == kPhHead) {
                 EpiLogits lg{a.logits, a.am_val, a.am_idx, a.am_ticket, a.st, a.tok_hist, a.max_seq, true};
+                lg.v0 = a.v0;
+                lg.tp_rank = a.tp_rank;
+                lg.tp_world = a.tp_world;
+                lg.tag = tag;
+                lg.xch = a.tp_xch;
+                lg.xch_off = 2 * (size_t)a.tp_world * a.D;
                 SEpiLogits{lg}.end(est, lane);  // the last CTA advances the sequence (and its step count)
             } else if (lane == 0) {
                 red_add_release_gpu(a.cnt + p, 1u);  // the warp's writes are ordered by the __syncwarp above

@@ -55,7 +55,11 @@ assert C.sizeof(ModelConfig) == 36
 
 
 class EngineOptions(C.Structure):
-    _fields_ = [("rope_theta", C.c_float), ("reserved", C.c_uint32 * 7)]
+    _fields_ = [("rope_theta", C.c_float), ("tp_rank", C.c_uint32), ("tp_world", C.c_uint32),
+                ("reserved", C.c_uint32 * 5)]
+
+
+BT_TP_HANDLE_BYTES = 64
 
 
 class TensorView(C.Structure):
@@ -99,11 +103,14 @@ SIGNATURES = {
     "bt_engine_decode": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32, _vp]),
     "bt_engine_set_taps": (_i32, [_vp, _i32]),
     "bt_engine_read_taps": (_i32, [_vp, _vp]),
+    "bt_engine_tp_handle": (_i32, [_vp, _vp]),
+    "bt_engine_tp_connect": (_i32, [_vp, _vp]),
     "bt_engine_begin": (_i32, [_vp, _vp, _vp, _u32, _u32]),
     "bt_engine_steps": (_i32, [_vp, _vp, _u32, _vp]),
     "bt_engine_stream": (_vp, [_vp]),
     "bt_engine_profile": (_i32, [_vp, _vp, _u32, _vp]),
     "bt_kv_state": (_i32, [_vp, _vp, _vp, _vp]),
+    "bt_kv_inject_stall": (_i32, [_vp]),
     "bt_kv_step_info": (_i32, [_vp, _u32, _vp, _vp]),
 }
 

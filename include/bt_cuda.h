@@ -68,8 +68,19 @@ typedef struct bt_model_config {
 /* Engine options that the reference hard-codes. */
 typedef struct bt_engine_options {
     float    rope_theta;   /* 10000.0f in kernels/cpu_ref.hpp:40; 500000 for Llama-3 shapes */
-    uint32_t reserved[7];
+    /* Tensor parallelism (no counterpart in the reference): this engine is rank
+     * tp_rank of tp_world <= 8 GPUs, one process per GPU.  0 or 1: the whole
+     * model on one GPU.  Rank r holds heads and KV heads [r H/W, (r+1) H/W),
+     * the same FFN share of gate/up rows and of down's input columns, o-proj's
+     * input columns of its heads, and vocab rows [r ceil(V/W), ...) of the
+     * head matrix; embeddings and norms are whole on every rank. */
+    uint32_t tp_rank;
+    uint32_t tp_world;
+    uint32_t reserved[5];
 } bt_engine_options;
+
+/* Bytes of a tensor-parallel exchange handle (a CUDA IPC memory handle). */
+#define BT_TP_HANDLE_BYTES 64
 
 /* One tensor of a model, as the .btmodel file stores it
  * (models/model_importer.cpp:27-41): fp32 for embeddings and norms, an array
@@ -263,8 +274,33 @@ BT_API void* bt_engine_stream(bt_engine* e);
  * device time of each kernel kind into ms_by_kind[6] = {qkv, attention,
  * o-proj, gate/up, down, head}.  Advances the sequence like bt_engine_steps. */
 BT_API int bt_engine_profile(bt_engine* e, bt_kv* kv, uint32_t n_steps, float* ms_by_kind);
-/* Position, current token and last argmax of the sequence (host copy). */
+/* Position, current token and last argmax of the sequence (host copy).
+ * Returns BT_ERR_DEVICE_TIMEOUT (outputs still filled) when a device wait of
+ * an earlier step expired. */
 BT_API int bt_kv_state(bt_kv* kv, uint32_t* pos, uint32_t* token, uint32_t* last_argmax);
+/* Tensor parallelism, after bt_engine_create with tp_world > 1 and before the
+ * first decode step: every rank writes its exchange handle
+ * (BT_TP_HANDLE_BYTES bytes) with bt_engine_tp_handle, the ranks gather the
+ * handles in rank order (torch.distributed, MPI, a file, ...), and every rank
+ * passes all tp_world handles to bt_engine_tp_connect, which maps the other
+ * ranks' buffers (CUDA IPC over NVLink).  The decode step then adds o-proj's
+ * and down's partial sums across the ranks inside the persistent kernel
+ * (every rank stores its row tiles into every rank's buffer and adds all ranks'
+ * in rank order) and agrees on the greedy token the same way; all ranks must
+ * run the same calls in the same order.  Logits of bt_engine_forward_token
+ * are this rank's vocab rows only (written at their offset). */
+BT_API int bt_engine_tp_handle(bt_engine* e, void* handle);
+BT_API int bt_engine_tp_connect(bt_engine* e, const void* handles);
+/* Fault injection on the host, for tests of the device timeouts (no
+ * counterpart in the reference): sets the sequence's device step count so
+ * that the phase barriers of its next persistent-kernel step can never be
+ * reached.  That step's waits then expire after their 2 s limit, the kernel
+ * finishes (every later wait of the step returns at once), and the error flag
+ * is set for bt_kv_state / bt_engine_decode to report.  No GPU fault and no
+ * hang: the context stays usable, and bt_engine_begin or
+ * bt_engine_forward_token resets the state.  BT_ERR_INVALID_ARGUMENT when the
+ * engine runs the launch-per-operation step. */
+BT_API int bt_kv_inject_stall(bt_kv* kv);
 /* Kernel launches of one decode step and the algorithmic HBM bytes it moves
  * when the step processes position context-1: weights (int8 + fp32 scales),
  * norms, one embedding row, KV read of `context` positions and the KV write. */

@@ -213,3 +213,32 @@ def test_tinyllama_shape_gqa(cuda, oracle):
         if lg is not None:
             assert_close_act(lg, lo, f"logits pos {p}")
         tok = int(np.argmax(lo))
+
+
+def test_device_wait_expiry_reports_timeout(cuda, tiny):
+    """Failure detection without a GPU fault: the host makes the phase barriers
+    of the next step unreachable (bt_kv_inject_stall), the step's bounded
+    device waits expire after 2 s, the kernel finishes, and the host reads
+    BT_ERR_DEVICE_TIMEOUT.  The context stays usable: a fresh sequence on the
+    same engine then decodes the same tokens as before the injection."""
+    import time
+    from blocktensor_b200 import native
+
+    cfg, ocfg, m, eng = tiny
+    g = np.load(os.path.join(GOLDEN, "tiny_c0.npz"))
+    prompt = [int(t) for t in g["prompt"]]
+    kv = cuda.KVCache(eng, 64)
+    clean = eng.decode(kv, prompt, n_gen=8)
+
+    eng.begin(kv, prompt)
+    kv.inject_stall()
+    t0 = time.time()
+    eng.steps(kv, 1)
+    with pytest.raises(native.CudaBackendError) as ei:
+        kv.state()
+    assert ei.value.code == native.BT_ERR_DEVICE_TIMEOUT
+    assert 1.5 < time.time() - t0 < 30.0, "the expiry should come from the 2 s device wait limit"
+
+    again = eng.decode(kv, prompt, n_gen=8)  # begin() resets the state and its error flag
+    assert list(again) == list(clean)
+    kv.state()
