@@ -216,14 +216,15 @@ int alloc_units(bt_engine* e, uint8_t** out, uint32_t M, uint32_t K, const char*
 
 // Shape of the persistent step kernel: head dims per lane, ring depth, shared
 // memory (ring + a scratch area for digits or attention partials).  Configs
-// whose query heads per KV head do not fit the kernel's registers use the
+// whose attention partials leave no room for a two-stage ring use the
 // launch-per-kernel step.
 int plan_step(bt_engine* e) {
     const auto& c = e->lc;
     const uint32_t hd = c.head_dim, GQ = c.num_heads / c.num_kv_heads;
     e->step_nv = hd <= 64 ? 2 : hd <= 128 ? 4 : 8;
     // phases 5 L + 1 < 1024: the phase index is the low 10 bits of the split partials' tags
-    e->step_ok = GQ * e->step_nv <= 16 && hd % e->step_nv == 0 && 5 * c.num_layers + 1 < 1024;
+    // (query heads per KV head beyond 16 / NV are taken in several passes over the keys)
+    e->step_ok = hd % e->step_nv == 0 && 5 * c.num_layers + 1 < 1024;
     uint32_t kmax = c.dim > c.hidden_dim ? c.dim : c.hidden_dim;
     if (qd(c) > kmax) kmax = qd(c);
     const size_t img_bytes = 2 * (size_t)mma_xstride(kmax) + ((kmax / 32) * 4 + 15) / 16 * 16;  // digits + block scales

@@ -360,7 +360,8 @@ template <int NV, int GQM, typename KVT>
 __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint32_t tid, uint8_t* img, uint32_t tag,
                            bool& ok) {
     // GQM: query heads per KV head held in registers; B: keys per batch and warp
-    constexpr int BW = 16 / RowWords<NV, KVT>::W;
+    // (half the batch when several query heads share the keys: their registers)
+    constexpr int BW = 16 / RowWords<NV, KVT>::W / (GQM > 1 ? 2 : 1);
     constexpr int B = BW > 8 ? 8 : (BW < 2 ? 2 : BW);
     const uint32_t lane = tid & 31, w = tid >> 5, G = gridDim.x;
     const uint32_t HD = a.hd, GQ = a.GQ, S = a.S_att;
@@ -378,6 +379,10 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
         const uint32_t kvh = it / S, sidx = it % S;
         const uint32_t Lk = (c + S - 1) / S;
         const uint32_t t0 = sidx * Lk, t1 = min(c, t0 + Lk);
+        const KVT* kb = kl + (size_t)kvh * a.max_seq * HD + d0;
+        const KVT* vb = vl + (size_t)kvh * a.max_seq * HD + d0;
+        // query heads g0 .. g0 + GQM - 1 of this KV head per pass (K/V re-read from L2 by later passes)
+        for (uint32_t g0 = 0; g0 < GQ; g0 += GQM) {
         float qv[GQM][NV], o[GQM][NV], m[GQM], ls[GQM];
 #pragma unroll
         for (int g = 0; g < GQM; ++g) {
@@ -386,11 +391,9 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
 #pragma unroll
             for (int i = 0; i < NV; ++i) {
                 o[g][i] = 0.0f;
-                qv[g][i] = ((uint32_t)g < GQ && active) ? __ldcg(a.q + (size_t)(kvh * GQ + g) * HD + d0 + i) : 0.0f;
+                qv[g][i] = (g0 + g < GQ && active) ? __ldcg(a.q + (size_t)(kvh * GQ + g0 + g) * HD + d0 + i) : 0.0f;
             }
         }
-        const KVT* kb = kl + (size_t)kvh * a.max_seq * HD + d0;
-        const KVT* vb = vl + (size_t)kvh * a.max_seq * HD + d0;
         for (uint32_t base = t0 + w; base < t1; base += B * kDigitWarps) {
             RowWords<NV, KVT> kr[B], vr[B];
 #pragma unroll
@@ -406,7 +409,7 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
             }
 #pragma unroll
             for (int g = 0; g < GQM; ++g) {
-                if ((uint32_t)g >= GQ) break;
+                if (g0 + g >= GQ) break;
                 float sc[B];
                 float mb = -INFINITY;
 #pragma unroll
@@ -438,12 +441,13 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
             }
         }
         // warp partials -> shared memory
-        for (uint32_t g = 0; g < GQ && g < (uint32_t)GQM; ++g) {
-            float* p = wm + ((size_t)w * GQ + g) * pstride;
+        for (uint32_t g = 0; g0 + g < GQ && g < (uint32_t)GQM; ++g) {
+            float* p = wm + ((size_t)w * GQ + g0 + g) * pstride;
             if (lane == 0) { p[0] = m[g]; p[1] = ls[g]; }
 #pragma unroll
             for (int i = 0; i < NV; ++i)
                 if (active) p[2 + d0 + i] = o[g][i];
+        }
         }
         digit_sync();
         // CTA partial of this split.  The CTA of split 0 keeps its own and merges the others (:148-184),

@@ -181,6 +181,7 @@ def test_gqa_theta_vs_oracle(cuda, oracle, kv_fp16):
     eng = cuda.TransformerEngine(cfg, rope_theta=500000.0)
     eng.generate(seed=21, sigma=0.02)
     kv = cuda.KVCache(eng, 300, cuda.BT_KV_FP16 if kv_fp16 else cuda.BT_KV_FP32)
+    assert kv.step_info(1)[0] == 1, "the persistent step kernel (query heads in groups of 16 / NV) runs this shape"
     okv = oracle.KV(ocfg, 300, fp16=kv_fp16)
     eng.set_taps(True)
     tok = 3
