@@ -155,9 +155,12 @@ def run_reference(args):
               f"(attention is <1% of the CPU step at contexts below 1k)")
     line = {
         "impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": done, "warmup": w, "ms_per_step": 1000.0 / tps, "higher_is_better": True, "scaling": "weak",
+        "steps": done, "warmup": w, "ms_per_step": 1000.0 / tps, "higher_is_better": True,
+        # the same one sequence as our arm (tensor parallel when N > 1, unless --replicas)
+        "scaling": "strong" if (args.gpus > 1 and not args.replicas) else "weak",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "llama2-7b-shaped int8 decode, batch 1 (reference CPU backend)",
+        "config": {"workload": "llama2-7b-shaped int8 decode, batch 1 (reference CPU backend, one host thread)",
+                   "model": "llama2-7b", "global_batch": 1, "parallelism": "reference CPU",
                    "vocab": 32000, "dim": 4096, "hidden": 11008, "layers": 32, "heads": 32, "head_dim": 128},
         "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": 1, "kind": kind, "sample": sample},
         "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
