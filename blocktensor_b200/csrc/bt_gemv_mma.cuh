@@ -24,18 +24,20 @@
 // CTAs is finished by the one that completes last, adding the CTAs' partial
 // sums in CTA order, so results are deterministic.
 //
-// Warp roles (320 threads): warp 0 produces (cp.async.bulk of 4-tile stages
-// into an mbarrier ring; weights never depend on the previous kernel, so under
-// programmatic dependent launch the ring fills while the previous kernel
-// drains); warps 1-4 issue the MMAs, warp 1+t for tile t of every stage (one
-// thread issuing a tcgen05.mma spends ~130 cycles on it, so a single issuer
-// could not keep up with HBM); warps 5-8 read the digit sums from tensor
-// memory (warp w reads TMEM lanes 32 (w%4) .. +31, all four tiles of a stage
-// with one load) and accumulate; warp 9 finishes each row tile (cross-CTA
-// merge, epilogue).  Warps 1-9 build the digits first.  Warp 1 owns the tensor
-// memory.  No thread loads weights into registers: the tensor cores read them
-// from the ring.  All waits are bounded (2 s); an expired wait sets *err and
-// the CTA still finishes and frees its tensor memory.
+// Warp roles (320 threads): warp 0 produces (cp.async.bulk of 8-tile, 36 KB
+// stages into an mbarrier ring; weights never depend on the previous kernel,
+// so under programmatic dependent launch the ring fills while the previous
+// kernel drains); warps 1-4 issue the MMAs, warp 1+t for tiles t and t+4 of
+// every stage (one thread issuing tcgen05.mma + commit spends ~390 cycles per
+// MMA, so a single issuer could not keep up with HBM); warps 5-8 read the
+// digit sums from tensor memory (warp w reads TMEM lanes 32 (w%4) .. +31, all
+// eight tiles of a stage with one load) and accumulate; warp 9 finishes each
+// row tile (cross-CTA merge, epilogue).  Stages are 36 KB because every stage
+// costs ~0.4 us of mbarrier hand-offs between the roles whatever its size.
+// Warps 1-9 build the digits first.  Warp 1 owns the tensor memory.  No
+// thread loads weights into registers: the tensor cores read them from the
+// ring.  All waits are bounded (2 s); an expired wait sets *err and the CTA
+// still finishes and frees its tensor memory.
 #pragma once
 
 #include "bt_common.cuh"
@@ -86,7 +88,7 @@ struct SplitScratch {
 struct MmaShape {
     uint32_t NS;           // ring stages
     uint32_t xstride;      // bytes between the two digit arrays (K halves)
-    uint32_t tmem_cols;    // power of two >= 32 * NS
+    uint32_t tmem_cols;    // power of two >= 64 * NS (8 columns per tile)
 };
 
 // ---------------------------------------------------------------- prologues
