@@ -1,7 +1,8 @@
 """Tensor-parallel decode against the single-GPU engine, one process per GPU.
 
 Run under torchrun (``python -m torch.distributed.run --nproc-per-node W
---master-addr 127.0.0.1 --master-port P -m blocktensor_b200.tp_check OUT.json``).
+--master-addr 127.0.0.1 --master-port P -m blocktensor_b200.tp_check OUT.json
+[mha|gqa]``).
 Every rank builds its share of the same synthetic model, the ranks exchange
 their handles over a gloo process group and decode a prompt plus greedy
 tokens; rank 0 then decodes the same sequence with the whole model on its
@@ -17,14 +18,18 @@ import sys
 
 import numpy as np
 
-# D 512, 8 heads of 64 (and 8 KV heads), FFN 1536, 4 layers, vocab 4096: every
-# rank holds whole heads and whole 32-blocks at 2, 4 and 8 GPUs
-CONFIG = dict(vocab=4096, dim=512, hidden=1536, layers=4, heads=8, kv_heads=8, head_dim=64, max_seq=128)
+# D 512, 8 heads of 64, FFN 1536, 4 layers, vocab 4096: every rank holds whole
+# heads and whole 32-blocks at 2, 4 and 8 GPUs ("mha": 8 KV heads); "gqa": 4
+# KV heads, 2 query heads per KV head on every rank (2 and 4 GPUs)
+CONFIGS = {
+    "mha": dict(vocab=4096, dim=512, hidden=1536, layers=4, heads=8, kv_heads=8, head_dim=64, max_seq=128),
+    "gqa": dict(vocab=4096, dim=512, hidden=1536, layers=4, heads=8, kv_heads=4, head_dim=64, max_seq=128),
+}
 PROMPT = [17, 3051, 999, 2, 4000, 123, 77, 1024]
 N_GEN = 40
 
 
-def main(out_path: str) -> int:
+def main(out_path: str, shape: str = "mha") -> int:
     import torch
     import torch.distributed as dist
 
@@ -35,7 +40,7 @@ def main(out_path: str) -> int:
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
-    c = CONFIG
+    c = CONFIGS[shape]
     cfg = bt.model_config(c["vocab"], c["dim"], c["hidden"], c["layers"], c["heads"], c["kv_heads"],
                           c["head_dim"], c["max_seq"])
     eng = bt.TransformerEngine(cfg, device=local, tp_rank=rank, tp_world=world)
@@ -68,4 +73,4 @@ def main(out_path: str) -> int:
 
 
 if __name__ == "__main__":
-    sys.exit(main(sys.argv[1]))
+    sys.exit(main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "mha"))

@@ -30,15 +30,15 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_tp_decode_matches_single_gpu(cuda, world, tmp_path):
+@pytest.mark.parametrize("world,shape", [(2, "mha"), (4, "mha"), (8, "mha"), (2, "gqa"), (4, "gqa")])
+def test_tp_decode_matches_single_gpu(cuda, world, shape, tmp_path):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
     out = tmp_path / "tp.json"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
-           "-m", "blocktensor_b200.tp_check", str(out)]
+           "-m", "blocktensor_b200.tp_check", str(out), shape]
     r = subprocess.run(["timeout", "-k", "30", "240"] + cmd, cwd=ROOT, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     res = json.loads(out.read_text())
