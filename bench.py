@@ -109,6 +109,49 @@ def dist_env():
     return world, rank, local
 
 
+# ---------------------------------------------------------------- step-kernel timeline
+
+PHASE_KINDS = ("qkv", "attention", "oproj", "gateup", "down")
+
+
+def trace_summary(tr: np.ndarray, n_layers: int) -> dict:
+    """Per-phase latency breakdown of one step from bt_engine_read_trace ([P][G][8] ns).
+
+    For each phase kind, medians over the middle layers (microseconds):
+      dur      end of the previous phase -> end of this one (last CTA's release)
+      wait     end of the previous phase -> median CTA passing its counter wait
+      digits   counter wait -> input digits in shared memory (median CTA)
+      first    digits -> first row tile's sums at the finisher (median CTA)
+      tail     median CTA's end -> last CTA's end (imbalance and merge polls)
+      lead     producer's first copy of the phase -> the phase's end (how far ahead the weights stream)
+    """
+    t = tr.astype(np.float64)
+    P = t.shape[0]
+    t[t == 0] = np.nan
+    end = np.nanmax(t[:, :, 3], axis=1)
+    start = np.nanmedian(t[:, :, 0], axis=1)
+    out = {k: {"dur": [], "wait": [], "digits": [], "first": [], "tail": [], "lead": []} for k in PHASE_KINDS}
+    out["head"] = {"dur": [], "wait": [], "digits": [], "first": [], "tail": [], "lead": []}
+    for p in range(1, P):
+        kind = "head" if p == P - 1 else PHASE_KINDS[p % 5]
+        layer = p // 5
+        if kind != "head" and not (1 <= layer < n_layers - 1):
+            continue
+        d = out[kind]
+        d["dur"].append(end[p] - end[p - 1])
+        d["wait"].append(start[p] - end[p - 1])
+        d["digits"].append(np.nanmedian(t[p, :, 1] - t[p, :, 0]))
+        d["first"].append(np.nanmedian(t[p, :, 2] - t[p, :, 1]))
+        d["tail"].append(end[p] - np.nanmedian(t[p, :, 3]))
+        d["lead"].append(end[p] - np.nanmin(t[p, :, 4]))
+    res = {}
+    for k, d in out.items():
+        res[k] = {m: (round(float(np.nanmedian(v)) / 1000.0, 2) if len(v) and np.isfinite(np.nanmedian(v)) else None)
+                  for m, v in d.items()}
+    res["step_us"] = round(float((np.nanmax(t[:, :, 3]) - np.nanmin(t[:, :, 0])) / 1000.0), 1)
+    return res
+
+
 # ---------------------------------------------------------------- CPU reference
 
 def cpu_reference_tokens_per_s(n_tokens: int, warmup: int, budget_s: float, log=print):
@@ -191,7 +234,7 @@ def run_ours(args):
 
     shape = args.model
     prompt_len, W, K = args.prompt, args.warmup, args.steps
-    max_seq = prompt_len + W + K + args.e2e_steps + args.profile_steps + 2
+    max_seq = prompt_len + W + K + args.e2e_steps + args.profile_steps + 3
     cfg = synthetic.config(shape, max_seq)
     if args.layers:
         # truncated depth, for small profiler captures only (never a bench line)
@@ -286,6 +329,16 @@ def run_ours(args):
         prof = eng.profile(kv, args.profile_steps)
         breakdown = {k: round(v / args.profile_steps * 1000.0, 1) for k, v in prof.items()}  # us per step
 
+    # optional diagnostic: per-phase device timestamps of one more step (not timed)
+    timeline = None
+    if args.trace:
+        eng.set_trace(True)
+        eng.steps(kv, 1)
+        torch.cuda.synchronize()
+        timeline = trace_summary(eng.read_trace(), cfg.num_layers)
+        eng.set_trace(False)
+        log("[ours] phase timeline (us): " + json.dumps(timeline))
+
     # DRAM bytes per launch of the step kernel from an ncu capture (profiles/), scaled to this model
     traffic = None
     tfile = os.path.join(ROOT, "profiles", "decode_step_traffic.json")
@@ -324,7 +377,7 @@ def run_ours(args):
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": peak_kind, "bytes_per_launch": bytes_avg,
                          "us_per_launch": ms_step * 1000.0, "traffic": traffic,
-                         "launch_per_op_breakdown_us": breakdown},
+                         "launch_per_op_breakdown_us": breakdown, "phase_timeline_us": timeline},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 32,
                     "d2h_bytes_per_step": vocab_local * 4 + 32,
                     "api": "bt_engine_forward_token(host token, host logits)"},
@@ -352,6 +405,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="also time the launch-per-operation step (per-kernel breakdown, diagnostic)")
+    ap.add_argument("--trace", action="store_true",
+                    help="also record one step's per-phase device timestamps (diagnostic, untimed)")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: N independent sequences (one per GPU) instead of tensor parallelism")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -122,6 +122,16 @@ def gemv_q8_units(units, x, M: int, K: int, stream=None, out=None):
     return y
 
 
+def gemm_q8_units(units, x, M: int, K: int, stream=None, out=None):
+    """Y = X W^T for X [T, K] on the unit layout (the tensor-core GEMM of prefill / batched decode)."""
+    torch = _torch()
+    x2 = x.reshape(-1, K).contiguous()
+    T = x2.shape[0]
+    y = out if out is not None else torch.empty((T, M), dtype=torch.float32, device=x.device)
+    call("bt_cuda_gemm_q8_units", _dev_ptr(units), _dev_ptr(x2), _dev_ptr(y), M, K, T, _stream(stream))
+    return y
+
+
 def gemv_q8(qs, scales, x, stream=None, out=None):
     """y[b] = W x[b] for x of shape [B, K] (B <= 16), W in the device layout."""
     torch = _torch()
@@ -262,6 +272,18 @@ class TransformerEngine:
         call("bt_engine_decode", self._h, kv.handle, p.ctypes.data, len(p), pos0, n_gen, out.ctypes.data)
         return out
 
+    def prefill(self, kv: "KVCache", prompt: Sequence[int], pos0: int = 0):
+        """bt_engine_prefill: all prompt positions but the last as batched GEMMs; the next
+        step processes the last prompt token."""
+        p = np.ascontiguousarray(np.asarray(prompt, dtype=np.uint32))
+        call("bt_engine_prefill", self._h, kv.handle, p.ctypes.data, len(p), pos0)
+
+    def generate_tokens(self, kv: "KVCache", prompt: Sequence[int], n_gen: int, pos0: int = 0) -> np.ndarray:
+        """As decode(), with the prompt prefilled by batched GEMMs (bt_engine_prefill)."""
+        self.prefill(kv, prompt, pos0)
+        self.steps(kv, 1 + n_gen)
+        return kv.read_tokens(pos0, len(prompt) + n_gen + 1)
+
     def tp_handle(self) -> bytes:
         """This rank's exchange handle (tensor parallelism; see tp.connect)."""
         buf = C.create_string_buffer(BT_TP_HANDLE_BYTES)
@@ -283,6 +305,23 @@ class TransformerEngine:
         out = np.zeros((c.num_layers, c.dim), np.float32)
         call("bt_engine_read_taps", self._h, out.ctypes.data)
         return out
+
+    def set_trace(self, enable: bool = True):
+        """Per-phase device timestamps of every later step (bt_engine_set_trace)."""
+        call("bt_engine_set_trace", self._h, int(enable))
+
+    def read_trace(self) -> np.ndarray:
+        """The last step's timestamps, [5 L + 1][SMs][8] uint64 nanoseconds (0: not recorded)."""
+        P = 5 * self.config.num_layers + 1
+        n = P * self.num_sms * 8
+        out = np.zeros(n, np.uint64)
+        call("bt_engine_read_trace", self._h, out.ctypes.data, n)
+        return out.reshape(P, self.num_sms, 8)
+
+    @property
+    def num_sms(self) -> int:
+        import torch
+        return torch.cuda.get_device_properties(self.device).multi_processor_count
 
     def begin(self, kv: "KVCache", prompt: Sequence[int], pos0: int = 0):
         p = np.ascontiguousarray(np.asarray(prompt, dtype=np.uint32))
@@ -338,6 +377,12 @@ class KVCache:
         v = np.zeros(n, np.float32)
         call("bt_kv_read_layer", self._h, layer, k.ctypes.data, v.ctypes.data)
         return k, v
+
+    def read_tokens(self, pos0: int, n: int) -> np.ndarray:
+        """Token consumed at positions pos0 .. pos0 + n - 1 (bt_kv_read_tokens)."""
+        out = np.zeros(n, np.uint32)
+        call("bt_kv_read_tokens", self._h, pos0, n, out.ctypes.data)
+        return out
 
     def state(self):
         pos, tok, am = C.c_uint32(), C.c_uint32(), C.c_uint32()

@@ -16,8 +16,9 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libbt_cuda.so")
 
-SOURCES = ["bt_quant.cu", "bt_prims.cu", "bt_engine.cu", "bt_noalloc.cu"]
-HEADERS = ["bt_common.cuh", "bt_gemv.cuh", "bt_gemv_mma.cuh", "bt_ptx.cuh", "bt_attention.cuh", "bt_step.cuh", "bt_internal.h"]
+SOURCES = ["bt_quant.cu", "bt_prims.cu", "bt_engine.cu", "bt_noalloc.cu", "bt_prefill.cu"]
+HEADERS = ["bt_common.cuh", "bt_gemv.cuh", "bt_gemv_mma.cuh", "bt_ptx.cuh", "bt_attention.cuh", "bt_step.cuh",
+           "bt_gemm.cuh", "bt_engine_impl.h", "bt_internal.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr",

@@ -31,131 +31,9 @@
 
 using namespace bt;
 
-// ---------------------------------------------------------------- engine objects
-
-// Matrices in the 4608-byte tile layout of bt_gemv_mma.cuh (rows padded to 128).
-struct LayerDev {
-    uint8_t* qkv;   // [D + 2 KVD] x D, q and k rows as RoPE pairs (i, i + hd/2) of each head
-    uint8_t* o;     // D x D
-    uint8_t* gu;    // 2F x D, (gate, up) rows interleaved
-    uint8_t* d;     // D x F
-    float* attn_norm;
-    float* ffn_norm;
-};
-
-struct bt_engine {
-    int device = 0;
-    bt_model_config cfg{};  // the model
-    // this GPU's share of it (tensor parallelism over tp_world GPUs; the whole model when 1):
-    // heads, KV heads, FFN rows and head-matrix (vocab) rows of rank tp_rank, dim unchanged
-    bt_model_config lc{};
-    uint32_t tp_rank = 0, tp_world = 1;
-    uint32_t v0 = 0;  // first vocab row of this rank
-    uint64_t* tp_xbuf = nullptr;     // exchange buffer of this rank (own allocation, shared by IPC)
-    size_t tp_bytes = 0;
-    uint64_t** tp_peers = nullptr;   // [tp_world] every rank's exchange buffer as mapped here (device array)
-    std::vector<void*> tp_opened;    // peer buffers opened by IPC
-    bool tp_ready = false;
-    float theta = 10000.0f;
-    cudaStream_t stream = nullptr;
-    bool pdl = true;
-    bool use_graph = true;
-    uint32_t prefetch_bytes = 98304;  // L2 prefetch of the next GEMV's weights, per CTA
-    // persistent step kernel (one launch per token); the launch-per-kernel step stays for profiling
-    bool use_step = true;
-    bool step_ok = false;
-    uint32_t step_nv = 0, step_ns = 0, step_xstride = 0, step_tmem = 0, step_scratch_off = 0;
-    size_t step_smem = 0;
-    StepLayer* d_layers = nullptr;  // device copy of the per-layer matrix table
-    uint8_t* step_img[2] = {nullptr, nullptr};  // digit images of GEMV inputs, by phase parity
-    float* step_ssp[2] = {nullptr, nullptr};    // row-tile sums of x^2, by phase parity
-    uint32_t num_sms = 148;
-    bool taps_on = false;
-    std::vector<void*> allocs;
-    std::vector<LayerDev> layers;
-    float* embed = nullptr;
-    float* out_norm = nullptr;
-    uint8_t* head = nullptr;  // V x D units
-    // partial sums of row tiles cut between CTAs of a GEMV ([num_sms][2][128] floats, or 64-bit tagged
-    // words in the step kernel) + one ticket per row tile (standalone GEMVs)
-    float* split_part = nullptr;
-    uint32_t* split_ticket = nullptr;
-    // activations
-    float* x = nullptr;
-    float* q = nullptr;
-    float* attn = nullptr;
-    float* act = nullptr;
-    float* logits = nullptr;
-    float* taps = nullptr;
-    // argmax scratch
-    float* am_val = nullptr;
-    uint32_t* am_idx = nullptr;
-    uint32_t* am_ticket = nullptr;
-    bool loaded = false;
-    std::vector<bt_kv*> kvs;  // caches created on this engine and not yet destroyed
-};
-
-struct bt_kv {
-    bt_engine* e = nullptr;
-    uint32_t max_seq = 0;
-    int dtype = BT_KV_FP32;
-    std::vector<void*> allocs;
-    void* k = nullptr;          // [L][KVH][max_seq][hd]
-    void* v = nullptr;
-    float2* rope = nullptr;     // [max_seq][hd/2]
-    DevState* st = nullptr;
-    uint32_t* tok_hist = nullptr;  // [max_seq + 1]
-    float* att_part = nullptr;
-    uint32_t* att_ticket = nullptr;
-    uint32_t splits = 1, lmax = 1;
-    DevState* h_st = nullptr;   // pinned staging
-    uint64_t host_pos = 0;      // position of the next step, mirrored on the host for bounds checks
-    cudaGraphExec_t graph = nullptr;
-    bool graph_taps = false;
-    // persistent step kernel: phase counters [5 L + 1], attention split partials and tickets
-    uint32_t* step_cnt = nullptr;
-    uint64_t* step_att_part = nullptr;  // tagged attention split partials of the step kernel
-    uint32_t step_S = 1;
-};
+#include "bt_engine_impl.h"
 
 namespace {
-
-struct DeviceGuard {
-    int prev = -1;
-    explicit DeviceGuard(int dev) {
-        cudaGetDevice(&prev);
-        if (prev != dev) cudaSetDevice(dev);
-    }
-    ~DeviceGuard() {
-        int cur = -1;
-        cudaGetDevice(&cur);
-        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
-    }
-};
-
-template <typename T>
-int dev_alloc(std::vector<void*>& list, T** out, size_t count, const char* what) {
-    void* p = nullptr;
-    const size_t bytes = count * sizeof(T);
-    cudaError_t e = cudaMalloc(&p, bytes ? bytes : 16);
-    if (e != cudaSuccess) {
-        cudaGetLastError();
-        return fail(e == cudaErrorMemoryAllocation ? BT_ERR_OUT_OF_MEMORY : BT_ERR_CUDA,
-                    std::string("cudaMalloc(") + what + ", " + std::to_string(bytes) + " B): " + cudaGetErrorString(e));
-    }
-    list.push_back(p);
-    *out = static_cast<T*>(p);
-    return BT_OK;
-}
-
-#define BT_TRY_ALLOC(list, ptr, count, what)                         \
-    do {                                                             \
-        int _rc = dev_alloc(list, ptr, count, what);                 \
-        if (_rc != BT_OK) return _rc;                                \
-    } while (0)
-
-uint32_t kvd(const bt_model_config& c) { return c.num_kv_heads * c.head_dim; }
-uint32_t qd(const bt_model_config& c) { return c.num_heads * c.head_dim; }  // query rows (dim without TP)
 
 int validate_config(const bt_model_config& c) {
     if (c.vocab_size == 0 || c.dim == 0 || c.hidden_dim == 0 || c.num_layers == 0 || c.num_heads == 0 ||
@@ -227,7 +105,7 @@ int plan_step(bt_engine* e) {
     e->step_ok = hd % e->step_nv == 0 && 5 * c.num_layers + 1 < 1024;
     uint32_t kmax = c.dim > c.hidden_dim ? c.dim : c.hidden_dim;
     if (qd(c) > kmax) kmax = qd(c);
-    const size_t img_bytes = 2 * (size_t)mma_xstride(kmax) + ((kmax / 32) * 4 + 15) / 16 * 16;  // digits + block scales
+    const size_t img_bytes = mma_digit_bytes(kmax);  // digits + block factors
     size_t scratch = img_bytes;
     const size_t attn = (size_t)kDigitWarps * GQ * (hd + 2) * 4;
     if (attn > scratch) scratch = attn;
@@ -244,6 +122,14 @@ int plan_step(bt_engine* e) {
     while (cols < ns * kStageTiles * kTileCols) cols <<= 1;
     e->step_tmem = cols;
     if (const char* v = std::getenv("BT_STEP_KERNEL")) e->use_step = (v[0] != '0');
+    if (const char* v = std::getenv("BT_STEP_PF")) {
+        const long n = std::atol(v);
+        if (n >= 0 && n <= 64) e->step_pf = (uint32_t)n;
+    }
+    if (const char* v = std::getenv("BT_STEP_EVICT_FIRST")) {
+        if (v[0] != '0') e->step_flags |= kStepFlagEvictFirst;
+        else e->step_flags &= ~kStepFlagEvictFirst;
+    }
     // the per-layer matrix table the kernel walks
     std::vector<StepLayer> tab(c.num_layers);
     const uint32_t D = c.dim, F = c.hidden_dim, Q = qd(c), QKV = Q + 2 * kvd(c);
@@ -349,6 +235,9 @@ int launch_step(bt_engine* e, bt_kv* kv, cudaStream_t s) {
     a.xstride = e->step_xstride;
     a.tmem_cols = e->step_tmem;
     a.scratch_off = e->step_scratch_off;
+    a.pf_stages = e->step_pf;
+    a.flags = e->step_flags;
+    a.trace = e->trace;
     const uint32_t grid = e->num_sms;
     cudaError_t ce;
     const bool f16 = kv->dtype == BT_KV_FP16;
@@ -1037,6 +926,39 @@ int bt_engine_decode(bt_engine* e, bt_kv* kv, const uint32_t* prompt, uint32_t n
 int bt_engine_set_taps(bt_engine* e, int enable) {
     if (!e) return fail(BT_ERR_INVALID_ARGUMENT, "null engine");
     e->taps_on = enable != 0;
+    return BT_OK;
+}
+
+int bt_engine_set_trace(bt_engine* e, int enable) {
+    if (!e) return fail(BT_ERR_INVALID_ARGUMENT, "null engine");
+    if (enable && !step_path(e)) return fail(BT_ERR_INVALID_ARGUMENT, "trace: the engine does not run the step kernel");
+    DeviceGuard guard(e->device);
+    BT_CUDA_CHECK(cudaStreamSynchronize(e->stream));
+    if (enable && !e->trace) {
+        const size_t n = (size_t)(5 * e->lc.num_layers + 1) * e->num_sms * kTraceSlots;
+        BT_TRY_ALLOC(e->allocs, &e->trace, n, "step trace");
+        BT_CUDA_CHECK(cudaMemset(e->trace, 0, n * sizeof(uint64_t)));
+    }
+    if (!enable && e->trace) {
+        for (size_t i = 0; i < e->allocs.size(); ++i)
+            if (e->allocs[i] == e->trace) {
+                e->allocs.erase(e->allocs.begin() + (long)i);
+                break;
+            }
+        cudaFree(e->trace);
+        e->trace = nullptr;
+    }
+    return BT_OK;
+}
+
+int bt_engine_read_trace(bt_engine* e, uint64_t* out, uint64_t n_words) {
+    if (!e || !out) return fail(BT_ERR_INVALID_ARGUMENT, "null argument");
+    if (!e->trace) return fail(BT_ERR_INVALID_ARGUMENT, "trace is off (bt_engine_set_trace)");
+    const uint64_t n = (uint64_t)(5 * e->lc.num_layers + 1) * e->num_sms * kTraceSlots;
+    if (n_words != n) return fail(BT_ERR_INVALID_ARGUMENT, "read_trace: n_words must be (5 L + 1) * SMs * 8");
+    DeviceGuard guard(e->device);
+    BT_CUDA_CHECK(cudaStreamSynchronize(e->stream));
+    BT_CUDA_CHECK(cudaMemcpy(out, e->trace, n * sizeof(uint64_t), cudaMemcpyDeviceToHost));
     return BT_OK;
 }
 

@@ -1,0 +1,450 @@
+// bt_gemm.cuh -- int8-weight GEMM over many tokens on the 5th-generation
+// tensor cores: prompt prefill and batched decode.
+//
+// Y[t][m] = sum_b scale[m][b] * sum_{i<32} q[m][32b+i] * x[t][32b+i] for T
+// token rows x[t], with the reference's per-row arithmetic
+// (quantization/quant_types.cpp:101-121): every 32-element block of every
+// token is written in 22-bit fixed point with its own exponent,
+// v = round(x * 2^e[t][b]), as three signed base-256 digits, exactly as the
+// decode GEMV does (bt_gemv_mma.cuh).  One tcgen05.mma (kind::i8, M = 128
+// weight rows, N = 96 digit rows = 32 tokens x 3 digits, K = 32) per weight
+// tile and token group gives every (row, token, digit) block dot product
+// exactly as int32 in tensor memory; the reader warps combine the digits in
+// fp32, multiply by the weight's block scale and the token's block factor
+// 2^-e, and accumulate over the blocks in order.  The weight scale varies per
+// (row, block), so the blocks cannot be summed inside the tensor core: the
+// per-block read-out on the CUDA cores (about ten operations per row, token
+// and block) bounds this kernel, not the tensor pipe.
+//
+// Layouts.  Weights: the 4608-byte tiles of bt_gemv_mma.cuh (128 rows x one
+// 32-column block, K-major no-swizzle canonical layout, then 128 fp32 scales).
+// Token digits ("token image"): per token group tg (32 tokens) and block b a
+// 3200-byte tile: K half 0 as 96 rows of 16 bytes (row 3 t + d = digit d of
+// token t: hi, mid, lo), K half 1 the same 1536 bytes later, then the 32
+// block factors 2^-e (NaN for a block holding an inf or NaN); tiles ordered
+// [tg][b], so the tiles of consecutive blocks of one group are contiguous.
+//
+// Work: a unit is (row tile g, token group tg); CTAs take units round robin,
+// consecutive units sharing a row tile (its weights are read from L2 by the
+// CTAs of the other token groups).  Per unit the producer streams the row
+// tile's weight tiles and the group's digit tiles in stages of 4 blocks; one
+// of two issuer threads issues each block's MMA into one of 5 tensor-memory
+// slots of 96 columns; 8 reader warps (4 lane quarters x 2 token halves) read
+// the slot, accumulate 16 tokens x their 32 rows in registers and, after the
+// unit's last block, run the epilogue on their 32 rows x 16 tokens (a warp's
+// 32 rows are one 32-element block of the output, so the epilogue can write
+// the next GEMM's token image directly).  All waits are bounded (2 s).
+#pragma once
+
+#include "bt_common.cuh"
+#include "bt_gemv_mma.cuh"
+#include "bt_ptx.cuh"
+
+namespace bt {
+
+constexpr uint32_t kGTok = 32;                            // tokens per group
+constexpr uint32_t kGN = 3 * kGTok;                       // digit rows per group (MMA N)
+constexpr uint32_t kGHalf = kGN * 16;                     // bytes of one K half of a digit tile
+constexpr uint32_t kGDTile = 2 * kGHalf + kGTok * 4;      // digit tile: 3200 bytes
+constexpr uint32_t kGStageBlocks = 4;
+constexpr uint32_t kGStageW = kGStageBlocks * kTileBytes;  // weight part of a stage
+constexpr uint32_t kGStageBytes = kGStageW + kGStageBlocks * kGDTile;  // 31232
+constexpr uint32_t kGSlots = 5;                           // tensor-memory slots of kGN columns
+constexpr int kGThreads = 352;                            // warp 0 producer, 1-2 issuers, 3-10 readers
+constexpr int kGIssuer0 = 1;
+constexpr int kGReader0 = 3;
+constexpr int kGReaders = 8;
+constexpr uint32_t kGMaxStages = 6;
+constexpr uint32_t kGSmem = kGMaxStages * kGStageBytes + 2 * 16 * 64 * 4;  // ring + SwiGLU exchange
+
+// Instruction descriptor: D s32, A and B s8, both K-major, N = 96, M = 128.
+constexpr uint32_t kIdescG = (2u << 4) | (1u << 7) | (1u << 10) | ((kGN >> 3) << 17) | ((128u >> 4) << 24);
+
+inline __host__ __device__ uint32_t token_groups(uint32_t T) { return (T + kGTok - 1) / kGTok; }
+inline __host__ __device__ size_t token_image_bytes(uint32_t T, uint32_t K) {
+    return (size_t)token_groups(T) * (K / 32) * kGDTile;
+}
+
+// Digits of block b of token t in a token image of NB blocks per token: warp-uniform call,
+// lane i holding element 32 b + i.
+__device__ __forceinline__ void token_digits(uint8_t* img, uint32_t NB, uint32_t t, uint32_t b, float p,
+                                             uint32_t lane) {
+    uint8_t* tile = img + ((size_t)(t / kGTok) * NB + b) * kGDTile;
+    const uint32_t ti = t % kGTok;
+    warp_digits(tile + ti * 48, kGHalf, reinterpret_cast<float*>(tile + 2 * kGHalf) + ti, p, lane);
+}
+
+// Per-token inputs of the epilogues.
+struct GemmTok {
+    uint32_t T;              // tokens
+    const uint32_t* pos;     // position of token t (RoPE, KV slot)
+    const uint32_t* seq;     // sequence (KV cache) of token t; null: all tokens in cache 0
+};
+
+// RMSNorm factor of token t from its per-block sums of squares ss[t][0..NB):
+// 1/sqrt(sum/K + eps) (kernels/cpu_ref.hpp:11-28), summed by the warp.
+__device__ __forceinline__ float token_inv(const float* ss, uint32_t NB, uint32_t K, float eps, uint32_t t,
+                                           uint32_t lane) {
+    float s = 0.0f;
+    for (uint32_t b = lane; b < NB; b += 32) s += __ldcg(ss + (size_t)t * NB + b);
+    s = warp_sum(s);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)K), eps)));
+}
+
+// ---------------------------------------------------------------- epilogues
+// rows(): called by each reader warp after a unit, lane = row r = row0 + lane
+// of its 32-row output block ob (= r / 32), v[i] the final value of token
+// tok0 + i (i < 16; tokens >= T are skipped by the caller's `valid` mask).
+// ex: 4 KB of shared memory of the warp's token half; bar(): named barrier of
+// the 4 warps of that half.
+
+// Y[t][m] (the standalone GEMM).
+struct GEpiStore {
+    float* y;
+    uint32_t M;
+    template <class Bar>
+    __device__ void rows(uint32_t r, uint32_t, uint32_t tok0, uint32_t nvalid, const float (&v)[16], uint32_t,
+                         uint32_t, float*, Bar) const {
+        if (r >= M) return;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            if ((uint32_t)i < nvalid) y[(size_t)(tok0 + i) * M + r] = v[i];
+    }
+};
+
+// x[t] += y (transformer_engine.cpp:191-195, 222-225); then the next GEMM's token
+// image of x * w_next and the per-block sums of x^2 for its RMSNorm.
+struct GEpiResidual {
+    float* x;              // [T][D]
+    const float* w_next;   // next RMSNorm weight
+    uint8_t* img_next;     // token image of the next GEMM (NB = D / 32)
+    float* ss_next;        // [T][D / 32]
+    float* tap;            // [T][D] copy of x (null: none)
+    uint32_t D;
+    template <class Bar>
+    __device__ void rows(uint32_t r, uint32_t ob, uint32_t tok0, uint32_t nvalid, const float (&v)[16],
+                         uint32_t lane, uint32_t, float*, Bar) const {
+        const uint32_t NB = D / 32;
+        if (ob >= NB) return;  // padding rows of the last row tile (warp-uniform: D is a multiple of 32)
+        const float w = w_next[r];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            if ((uint32_t)i >= nvalid) break;
+            const uint32_t t = tok0 + i;
+            float* xp = x + (size_t)t * D + r;
+            const float xn = __fadd_rn(__ldcg(xp), v[i]);
+            *xp = xn;
+            if (tap) tap[(size_t)t * D + r] = xn;
+            token_digits(img_next, NB, t, ob, xn * w, lane);
+            const float ss = warp_sum(xn * xn);
+            if (lane == 0) ss_next[(size_t)t * NB + ob] = ss;
+        }
+    }
+};
+
+// (gate, up) row pairs (2j, 2j+1): act[t][j] = silu(gate) * up (cpu_ref.hpp:74-79,
+// transformer_engine.cpp:212-215), then the down GEMM's token image of act.  A
+// warp holds 16 act values of a token, half a 32-block: the four warps of a
+// token half exchange them through shared memory and the warps of quarters 0
+// and 2 write the digits of the row tile's two act blocks.
+struct GEpiSwiGLU {
+    float* act;            // [T][F]
+    uint8_t* img_next;     // token image of the down GEMM (NB = F / 32)
+    uint32_t F;
+    template <class Bar>
+    __device__ void rows(uint32_t r, uint32_t, uint32_t tok0, uint32_t nvalid, const float (&v)[16], uint32_t lane,
+                         uint32_t q, float* ex, Bar bar) const {
+        // ex: [16 tokens][64 act values of the row tile]
+        bar();  // the previous unit's readers of ex are done
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float up = __shfl_down_sync(0xffffffffu, v[i], 1);
+            if ((lane & 1) == 0 && (uint32_t)i < nvalid) {
+                const float g = v[i];
+                const float a = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), up);
+                const uint32_t j = r >> 1;
+                if (j < F) act[(size_t)(tok0 + i) * F + j] = a;
+                ex[i * 64 + 16 * q + (lane >> 1)] = a;
+            }
+        }
+        bar();
+        if (q == 0 || q == 2) {
+            const uint32_t NB = F / 32;
+            const uint32_t ob = (r - lane) >> 6;  // act block of this warp pair: 2 g + q / 2
+            if (ob < NB) {
+#pragma unroll 1
+                for (uint32_t i = 0; i < nvalid; ++i)
+                    token_digits(img_next, NB, tok0 + i, ob, ex[i * 64 + 32 * (q >> 1) + lane], lane);
+            }
+        }
+    }
+};
+
+// q/k/v rows (RoPE pairs (i, i + hd/2) of each head adjacent, as the decode
+// layout), RoPE at each token's position and the K/V append (:117-146).
+template <typename KVT>
+struct GEpiQKV {
+    float* q;              // [T][DQ]
+    KVT* kc;               // [seq][L][KVH][max_seq][hd] (this layer's offset applied)
+    KVT* vc;
+    size_t seq_stride;     // elements between sequences
+    const float2* rope;    // [max_seq][hd/2]
+    GemmTok tk;
+    uint32_t DQ, KVD, hd, max_seq;
+    template <class Bar>
+    __device__ void rows(uint32_t r, uint32_t, uint32_t tok0, uint32_t nvalid, const float (&v)[16], uint32_t lane,
+                         uint32_t, float*, Bar) const {
+        const uint32_t half = hd >> 1;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float partner = __shfl_xor_sync(0xffffffffu, v[i], 1);
+            if ((uint32_t)i >= nvalid) continue;
+            const uint32_t t = tok0 + i;
+            const uint32_t pos = tk.pos[t];
+            if (pos >= max_seq) continue;
+            const size_t so = tk.seq ? (size_t)tk.seq[t] * seq_stride : 0;
+            if (r < DQ + KVD) {
+                const bool isq = r < DQ;
+                const uint32_t local = isq ? r : r - DQ;
+                const uint32_t h = local / hd, j = (local % hd) >> 1;
+                const float2 cs = rope[(size_t)pos * half + j];
+                float o;
+                uint32_t d;
+                if ((lane & 1) == 0) {  // first of the pair: a cos - b sin
+                    o = __fsub_rn(__fmul_rn(v[i], cs.x), __fmul_rn(partner, cs.y));
+                    d = j;
+                } else {                // second: a sin + b cos
+                    o = __fadd_rn(__fmul_rn(partner, cs.y), __fmul_rn(v[i], cs.x));
+                    d = j + half;
+                }
+                if (isq) q[(size_t)t * DQ + h * hd + d] = o;
+                else kc[so + ((size_t)h * max_seq + pos) * hd + d] = KVConv<KVT>::from_f(o);
+            } else if (r < DQ + 2 * KVD) {
+                const uint32_t local = r - DQ - KVD;
+                const uint32_t h = local / hd, d = local % hd;
+                vc[so + ((size_t)h * max_seq + pos) * hd + d] = KVConv<KVT>::from_f(v[i]);
+            }
+        }
+    }
+};
+
+// ---------------------------------------------------------------- kernel
+
+struct GemmIn {
+    const uint8_t* img;    // token image of the input, [NTG][NB][kGDTile]
+    const float* ss;       // per-block sums of squares [T][NB] of the RMSNorm input (null: no norm)
+    float eps;
+    uint32_t T;
+};
+
+template <class Epi>
+__global__ void __launch_bounds__(kGThreads, 1) gemm_digits_kernel(UnitW W, GemmIn in, Epi epi, uint32_t NS,
+                                                                   uint32_t* err) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full[kGMaxStages], empty[kGMaxStages];
+    __shared__ __align__(8) uint64_t tfull[kGSlots], tfree[kGSlots];
+    __shared__ uint32_t s_tmem;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t NB = W.K / kTileK, NTG = token_groups(in.T);
+    const uint32_t units = (W.Mp / kTileRows) * NTG;
+    const uint32_t nst = (NB + kGStageBlocks - 1) / kGStageBlocks;  // stages per unit
+    uint8_t* ring = smem;
+    float* exch = reinterpret_cast<float*>(smem + (size_t)kGMaxStages * kGStageBytes);
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kGReaders);
+        }
+        for (uint32_t s = 0; s < kGSlots; ++s) {
+            mbar_init(&tfull[s], 1);
+            mbar_init(&tfree[s], kGReaders);
+        }
+        fence_mbar_init();
+    }
+    if (warp == kGIssuer0) {
+        tmem_alloc(&s_tmem, 512);
+        tmem_relinquish();
+    }
+    tcgen05_fence_before();
+    __syncthreads();
+    tcgen05_fence_after();
+    const uint32_t tmem = s_tmem;
+
+    if (warp == 0) {
+        // ---------------- producer
+        if (lane == 0) {
+            uint32_t s = 0, ph = 0, issued = 0;
+            bool ok = true;
+            for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                const uint32_t g = u / NTG, tg = u % NTG;
+                for (uint32_t st = 0; st < nst; ++st) {
+                    if (issued >= NS && !(ok = mbar_wait(&empty[s], ph ^ 1, err))) break;
+                    const uint32_t b0 = st * kGStageBlocks, n = min(kGStageBlocks, NB - b0);
+                    mbar_expect_tx(&full[s], n * (kTileBytes + kGDTile));
+                    uint8_t* dst = ring + (size_t)s * kGStageBytes;
+                    bulk_g2s(dst, W.units + ((size_t)g * NB + b0) * kTileBytes, n * kTileBytes, &full[s]);
+                    bulk_g2s(dst + kGStageW, in.img + ((size_t)tg * NB + b0) * kGDTile, n * kGDTile, &full[s]);
+                    ++issued;
+                    if (++s == NS) { s = 0; ph ^= 1; }
+                }
+            }
+            const uint32_t first = issued > NS ? issued - NS : 0;
+            for (uint32_t j = first; j < issued; ++j) mbar_wait(&full[j % NS], (j / NS) & 1, nullptr);
+        }
+        return;
+    }
+
+    if (warp < kGReader0) {
+        // ---------------- issuers: warp 1 + i issues the blocks j with j % 2 == i
+        const uint32_t i = warp - kGIssuer0;
+        if (lane == 0) {
+            bool ok = true;
+            uint32_t s = 0, ph = 0, j = 0;
+            for (uint32_t u = blockIdx.x; u < units; u += gridDim.x) {
+                for (uint32_t st = 0; st < nst; ++st) {
+                    const uint32_t b0 = st * kGStageBlocks, n = min(kGStageBlocks, NB - b0);
+                    if (ok) ok = mbar_wait(&full[s], ph, err);
+                    tcgen05_fence_after();
+                    const uint8_t* stage = ring + (size_t)s * kGStageBytes;
+                    for (uint32_t k = 0; k < n; ++k, ++j) {
+                        if ((j & 1) != i) continue;
+                        const uint32_t slot = j % kGSlots, use = j / kGSlots;
+                        if (use > 0 && ok) ok = mbar_wait(&tfree[slot], (use - 1) & 1, err);
+                        tcgen05_fence_after();
+                        const uint64_t a = umma_desc(smem_u32(stage + k * kTileBytes), 128, 256);
+                        const uint64_t b = umma_desc(smem_u32(stage + kGStageW + k * kGDTile), kGHalf, 128);
+                        if (ok) umma_s8(tmem + slot * kGN, a, b, kIdescG, 0);
+                        umma_commit(&tfull[slot]);  // arrives once this MMA is complete
+                    }
+                    if (++s == NS) { s = 0; ph ^= 1; }
+                }
+            }
+        }
+        __syncwarp();
+        // tensor memory is freed after every reader is done with it
+        asm volatile("bar.sync 3, %0;" ::"n"(32 * (2 + kGReaders)) : "memory");
+        if (warp == kGIssuer0) {
+            tcgen05_fence_after();
+            tmem_dealloc(tmem, 512);
+        }
+        return;
+    }
+
+    // ---------------- readers: lane quarter q (TMEM lanes 32 q ..), token half h (tokens 16 h .. 16 h + 15)
+    const uint32_t q = warp & 3, h = (warp - kGReader0) >> 2;
+    const uint32_t row = 32 * q + lane;
+    const uint32_t taddr = tmem + ((32 * q) << 16) + 48 * h;
+    float* ex = exch + h * (16 * 64);
+    auto bar = [h]() { asm volatile("bar.sync %0, 128;" ::"r"(4 + h) : "memory"); };
+    bool ok = true;
+    uint32_t s = 0, ph = 0, j = 0;
+    for (uint32_t u = blockIdx.x; u < units; u += gridDim.x) {
+        const uint32_t g = u / NTG, tg = u % NTG;
+        float acc[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
+        for (uint32_t st = 0; st < nst; ++st) {
+            const uint32_t b0 = st * kGStageBlocks, n = min(kGStageBlocks, NB - b0);
+            const uint8_t* stage = ring + (size_t)s * kGStageBytes;
+            for (uint32_t k = 0; k < n; ++k, ++j) {
+                const uint32_t slot = j % kGSlots, use = j / kGSlots;
+                if (ok) ok = mbar_wait(&tfull[slot], use & 1, err);
+                tcgen05_fence_after();
+                uint32_t d[48];
+                tmem_ld32(taddr + slot * kGN, *reinterpret_cast<uint32_t(*)[32]>(d));
+                tmem_ld16(taddr + slot * kGN + 32, *reinterpret_cast<uint32_t(*)[16]>(d + 32));
+                const float sc = *reinterpret_cast<const float*>(stage + k * kTileBytes + kTileQBytes + row * 4);
+                const float4* bfp = reinterpret_cast<const float4*>(stage + kGStageW + k * kGDTile + 2 * kGHalf) + 4 * h;
+                float bf[16];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float4 f = bfp[i];
+                    bf[4 * i] = f.x; bf[4 * i + 1] = f.y; bf[4 * i + 2] = f.z; bf[4 * i + 3] = f.w;
+                }
+                tmem_wait_ld();
+                tcgen05_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tfree[slot]);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float y = fmaf(fmaf(small_i2f((int)d[3 * i]), 256.0f, small_i2f((int)d[3 * i + 1])), 256.0f,
+                                         small_i2f((int)d[3 * i + 2]));
+                    acc[i] = fmaf(sc * bf[i], y, acc[i]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the stage's shared memory
+            if (++s == NS) { s = 0; ph ^= 1; }
+        }
+        // ---------------- epilogue of the unit
+        const uint32_t tok0 = tg * kGTok + 16 * h;
+        const uint32_t nvalid = tok0 < in.T ? min(16u, in.T - tok0) : 0u;
+        if (in.ss) {
+            const uint32_t NBin = NB;
+#pragma unroll 1
+            for (uint32_t i = 0; i < 16; ++i) {
+                if (i >= nvalid) break;
+                const float inv = token_inv(in.ss, NBin, W.K, in.eps, tok0 + i, lane);
+#pragma unroll
+                for (int k = 0; k < 16; ++k)
+                    if ((uint32_t)k == i) acc[k] *= inv;
+            }
+        }
+        const uint32_t r = g * kTileRows + row;
+        epi.rows(r, r >> 5, tok0, nvalid, acc, lane, q, ex, bar);
+    }
+    tcgen05_fence_before();
+    asm volatile("bar.sync 3, %0;" ::"n"(32 * (2 + kGReaders)) : "memory");
+}
+
+// The token image of an input that no GEMM epilogue writes: src rows (or the
+// embedding rows of `tokens`) times the RMSNorm weight w (null: none), plus the
+// per-block sums of squares of the unweighted rows; x_out (non-null) receives
+// the rows themselves (the residual stream of layer 0).  One warp per (token, block).
+__global__ void __launch_bounds__(256) token_image_kernel(const float* __restrict__ src,
+                                                          const uint32_t* __restrict__ tokens,
+                                                          const float* __restrict__ w, uint32_t T, uint32_t K,
+                                                          uint8_t* img, float* ss, float* x_out) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t NB = K / 32;
+    const uint64_t item = (uint64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (item >= (uint64_t)T * NB) return;
+    const uint32_t t = (uint32_t)(item / NB), b = (uint32_t)(item % NB);
+    const float* row = tokens ? src + (size_t)tokens[t] * K : src + (size_t)t * K;
+    const uint32_t k = 32 * b + lane;
+    const float x = __ldcg(row + k);
+    if (x_out) x_out[(size_t)t * K + k] = x;
+    token_digits(img, NB, t, b, w ? x * w[k] : x, lane);
+    if (ss) {
+        const float s = warp_sum(x * x);
+        if (lane == 0) ss[(size_t)t * NB + b] = s;
+    }
+}
+
+// ---------------------------------------------------------------- host side
+
+inline uint32_t gemm_stages() { return (uint32_t)kGMaxStages; }
+
+template <class Epi>
+cudaError_t launch_gemm_digits(const UnitW& W, const GemmIn& in, const Epi& epi, uint32_t* err, uint32_t nsm,
+                               cudaStream_t s) {
+    if (W.K % kTileK || W.Mp % kTileRows || W.K == 0 || W.Mp == 0) return cudaErrorInvalidValue;
+    const uint32_t units = (W.Mp / kTileRows) * token_groups(in.T);
+    if (units == 0) return cudaSuccess;
+    auto kern = gemm_digits_kernel<Epi>;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGSmem);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    const uint32_t grid = units < nsm ? units : nsm;
+    return launch_pdl(kern, dim3(grid), dim3(kGThreads), (size_t)kGSmem, s, false, W, in, epi, gemm_stages(), err);
+}
+
+}  // namespace bt

@@ -2,15 +2,17 @@
 //
 // Arithmetic.  The reference computes y[r] = sum_b scale[r][b] * sum_{i<32}
 // q[r][32b+i] * x[32b+i] in fp32 (quantization/quant_types.cpp:101-121).  Here
-// x is first written as a 22-bit fixed-point vector v = round(x * 2^e) with one
-// power-of-two exponent e per vector (|v| <= 2^21), and v as three signed
+// every 32-element block b of x is first written in 22-bit fixed point,
+// v = round(x * 2^e_b) with the block's own power-of-two exponent e_b
+// (max |x| of the block times 2^e_b in [2^20, 2^21)), and v as three signed
 // base-256 digits hi/mid/lo.  One tcgen05.mma (kind::i8, M=128, N=8, K=32) per
 // 128-row x 32-column tile gives, for every row, the three digit dot products
 // sum_i q_i * digit_i exactly as int32 in tensor memory; they are combined in
-// fp32 ((256*hi + mid)*256 + lo), scaled by the block scale and accumulated in
-// fp32 across blocks, and 2^-e is applied at the end.  The only rounding
-// besides fp32 accumulation is x's quantisation step of 2^-21 relative to
-// max|x|.
+// fp32 ((256*hi + mid)*256 + lo), multiplied by the weight's block scale and
+// by 2^-e_b, and accumulated in fp32 across blocks.  The only rounding besides
+// fp32 accumulation is x's quantisation step of 2^-21 relative to the max |x|
+// of its own block, so a block of small values next to an outlier block keeps
+// its full precision.
 //
 // Layout (written by the pack kernel): rows in tiles of 128; a matrix is the
 // stream of its (row tile, 32-column block) tiles, row-tile-major.  A tile is
@@ -92,17 +94,28 @@ struct MmaShape {
 };
 
 // ---------------------------------------------------------------- prologues
-// Consumer threads build the digit fragments of the input vector.  load()
-// reads four consecutive elements (16-byte aligned), accumulates what the
-// prologue needs (sum of squares, max |p|) and returns p, the value before the
-// per-vector factor; factor() turns the sum of squares into that factor.
+// Digit threads build the input vector's digits.  load() reads four
+// consecutive elements (16-byte aligned), accumulates what the prologue needs
+// (sum of squares, max |p| as a bit pattern) and returns p, the value before
+// the per-vector factor; factor() turns the sum of squares into that factor.
+
+// Running max of |v| over the bit patterns: unlike fmaxf it keeps a NaN (whose
+// pattern is above inf's), so a block holding a NaN or inf is seen as one.
+__device__ __forceinline__ void amax4(float& mx, const float4& v) {
+    uint32_t m = __float_as_uint(mx);
+    m = max(m, __float_as_uint(fabsf(v.x)));
+    m = max(m, __float_as_uint(fabsf(v.y)));
+    m = max(m, __float_as_uint(fabsf(v.z)));
+    m = max(m, __float_as_uint(fabsf(v.w)));
+    mx = __uint_as_float(m);
+}
 
 struct MProCopy {
     const float* src;
     __device__ const float* base(uint32_t) const { return src; }
     __device__ float4 load(const float* s, uint32_t k, float&, float& mx) const {
         const float4 v = *reinterpret_cast<const float4*>(s + k);
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        amax4(mx, v);
         return v;
     }
     __device__ float factor(float, uint32_t) const { return 1.0f; }
@@ -127,7 +140,7 @@ struct MProNorm {
         ss = fmaf(v.w, v.w, ss);
         if (embed && blockIdx.x == 0) *reinterpret_cast<float4*>(x_out + k) = v;
         const float4 p = make_float4(v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w);
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(p.x), fabsf(p.y)), fmaxf(fabsf(p.z), fabsf(p.w))));
+        amax4(mx, p);
         return p;
     }
     __device__ float factor(float ss, uint32_t K) const {
@@ -143,14 +156,40 @@ __device__ __forceinline__ void digits3(int v, int& hi, int& mid, int& lo) {
     hi = (v1 - mid) >> 8;
 }
 
-// Digit arrays of the B operand: for each K half c (0, 1), block b's three
-// digit rows (hi, mid, lo; 16 bytes each = the 16 elements of that half) at
-// xb + c * xstride + 48 b.  The B tile of block b (N = 8 rows of 16 bytes per
-// K half) starts at its hi row: rows 3..7 are the next blocks' digits, which
-// only reach D columns 3..7, never read.  128 bytes of padding end each array.
+// Digit area of the B operand: for each K half c (0, 1), block b's three digit
+// rows (hi, mid, lo; 16 bytes each = the 16 elements of that half) at xb + c *
+// xstride + 48 b, then the block factors 2^-e_b as floats at 2 * xstride.  The
+// B tile of block b (N = 8 rows of 16 bytes per K half) starts at its hi row:
+// rows 3..7 are the next blocks' digits, which only reach D columns 3..7,
+// never read.  128 bytes of padding end each digit array.
+
+__device__ __forceinline__ uint32_t blk_off(uint32_t xstride) { return 2 * xstride; }
+
+// Block exponent e with max |p| * 2^e in [2^20, 2^21), so that round(p * 2^e)
+// fits 22 bits; finite = false for a block holding an inf or NaN.
+__device__ __forceinline__ int block_exponent(float am, bool& finite) {
+    finite = isfinite(am);
+    int e = 0;
+    if (am > 0.0f && finite) {
+        int ex;  // am = fr * 2^ex, fr in [0.5, 1)
+        if (am >= 1.17549435e-38f)
+            ex = ((__float_as_int(am) >> 23) & 255) - 126;
+        else
+            frexpf(am, &ex);
+        e = 21 - ex;
+        if (e > 149) e = 149;  // 2^-e stays representable
+    }
+    return e;
+}
+
+// 2^k for |k| <= 126, exactly.
+__device__ __forceinline__ float pow2i(int k) { return __int_as_float((127 + k) << 23); }
+
+// 2^-e for the block exponents above (subnormal below 2^-126).
+__device__ __forceinline__ float pow2neg(int e) { return e <= 126 ? pow2i(-e) : ldexpf(1.0f, -e); }
 
 // Writes the digits of one item (8 elements: block idx/4, elements 4 (idx%4)
-// + {0..3} of each K half).
+// + {0..3} of each K half), v = round(p * c1 * c2).
 __device__ __forceinline__ void pack_item(uint8_t* xb, uint32_t xstride, uint32_t idx, const float4& a,
                                           const float4& b, float c1, float c2) {
     const float va[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
@@ -173,68 +212,89 @@ __device__ __forceinline__ void pack_item(uint8_t* xb, uint32_t xstride, uint32_
             *reinterpret_cast<uint32_t*>(xb + c * xstride + blk * 48 + d * 16 + tig * 4) = r[d][c];
 }
 
-// Builds the digit arrays and returns the exponent e; *bad when the vector
-// holds an inf or NaN (the outputs are then NaN).  One global round trip: item
-// idx is loaded once into registers by digit thread idx % 288 (K <= 13824;
-// larger vectors load their tail twice).  Called by the 288 threads of warps
-// 1-9 (tid = 0..287); ends with the digits visible to the tensor cores.
+// round(p * 2^e) for |p * 2^e| <= 2^21 (round half to even, as cvt.rni).
+__device__ __forceinline__ int scaled_round(float p, int e) {
+    const float t = __fmul_rn(__fmul_rn(p, pow2i(e / 2)), pow2i(e - e / 2));
+    return __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
+}
+
+// One warp writes the digits of one 32-element block, lane i holding element i
+// (warp-uniform call).  The block's max |p| is one redux.sync on the bit
+// patterns (monotonic for non-negative floats; an inf or NaN anywhere makes
+// the block factor NaN, so it propagates to every output as in fp32
+// arithmetic); each lane packs its three digit bytes into one word and three
+// shuffles bring the next lanes' words for the 4-element digit words of lanes
+// 0, 4, ... .  hi_row: the block's hi digit row of K half 0 (16 bytes; the mid
+// and lo rows follow at +16 and +32, K half 1 at hi_row + half_stride);
+// factor: where the block factor 2^-e goes.
+__device__ __forceinline__ void warp_digits(uint8_t* hi_row, uint32_t half_stride, float* factor, float p,
+                                            uint32_t lane) {
+    const float am = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(p))));
+    bool finite;
+    const int e = block_exponent(am, finite);
+    const int v = finite ? scaled_round(p, e) : 0;
+    int hi, mid, lo;
+    digits3(v, hi, mid, lo);
+    const uint32_t w0 = ((uint32_t)hi & 255u) | (((uint32_t)mid & 255u) << 8) | (((uint32_t)lo & 255u) << 16);
+    const uint32_t w1 = __shfl_down_sync(0xffffffffu, w0, 1);
+    const uint32_t w2 = __shfl_down_sync(0xffffffffu, w0, 2);
+    const uint32_t w3 = __shfl_down_sync(0xffffffffu, w0, 3);
+    if ((lane & 3) == 0) {
+        // digit d of elements lane .. lane+3: byte d of w0, w1, w2, w3
+        const uint32_t a01 = __byte_perm(w0, w1, 0x5140), a23 = __byte_perm(w2, w3, 0x5140);  // hi, mid bytes
+        const uint32_t b01 = __byte_perm(w0, w1, 0x0062), b23 = __byte_perm(w2, w3, 0x0062);  // lo bytes
+        uint8_t* q = hi_row + (lane >> 4) * half_stride + (lane & 15);
+        *reinterpret_cast<uint32_t*>(q) = __byte_perm(a01, a23, 0x5410);        // hi
+        *reinterpret_cast<uint32_t*>(q + 16) = __byte_perm(a01, a23, 0x7632);   // mid
+        *reinterpret_cast<uint32_t*>(q + 32) = __byte_perm(b01, b23, 0x5410);   // lo
+    }
+    if (lane == 0) *factor = finite ? pow2neg(e) : __int_as_float(0x7fc00000);
+}
+
+// Builds the digit area of a whole input vector with one exponent per 32-element
+// block, and returns the per-vector factor (the RMSNorm factor; 1 without a
+// norm).  Item idx (8 elements) goes to digit thread idx % 288; the four items
+// of a block sit in four consecutive lanes, which share the block's max |p|
+// by two shuffles.  A block holding an inf or NaN gets a NaN factor, so every
+// output it reaches is NaN, as in fp32 arithmetic.  Called by the 288 threads
+// of the digit warps (tid = 0..287); ends with the digits visible to the
+// tensor cores.
 template <class Pro>
-__device__ int build_digits(const Pro& pro, uint32_t K, uint8_t* xb, uint32_t xstride, float* red, uint32_t tid,
-                            bool& bad) {
-    constexpr int R = 6;
+__device__ float block_digits(const Pro& pro, uint32_t K, uint8_t* xb, uint32_t xstride, float* red, uint32_t tid) {
     const float* s = pro.base(K);
     const uint32_t items = K >> 3;
-    float ss = 0.0f, mx = 0.0f;
-    float4 pa[R], pb[R];
-#pragma unroll
-    for (int i = 0; i < R; ++i) {
-        const uint32_t idx = tid + kDigitThreads * i;
-        if (idx < items) {
-            const uint32_t k = (idx >> 2) * 32 + (idx & 3) * 4;
-            pa[i] = pro.load(s, k, ss, mx);
-            pb[i] = pro.load(s, k + 16, ss, mx);
+    float ss = 0.0f;
+    for (uint32_t i0 = 0; i0 < items; i0 += kDigitThreads) {  // same trip count in every thread (shuffles below)
+        const uint32_t idx = i0 + tid;
+        const bool valid = idx < items;
+        const uint32_t k = (idx >> 2) * 32 + (idx & 3) * 4;
+        float4 pa = make_float4(0.f, 0.f, 0.f, 0.f), pb = pa;
+        float mx = 0.0f;
+        if (valid) {
+            pa = pro.load(s, k, ss, mx);
+            pb = pro.load(s, k + 16, ss, mx);
+        }
+        uint32_t mb = __float_as_uint(mx);
+        mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
+        mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 2));
+        bool finite;
+        const int e = block_exponent(__uint_as_float(mb), finite);
+        if (valid) {
+            pack_item(xb, xstride, idx, pa, pb, pow2i(e / 2), pow2i(e - e / 2));
+            if ((idx & 3) == 0)
+                *reinterpret_cast<float*>(xb + blk_off(xstride) + 4 * (idx >> 2)) =
+                    finite ? pow2neg(e) : __int_as_float(0x7fc00000);
         }
     }
-    for (uint32_t idx = tid + kDigitThreads * R; idx < items; idx += kDigitThreads) {
-        const uint32_t k = (idx >> 2) * 32 + (idx & 3) * 4;
-        pro.load(s, k, ss, mx);
-        pro.load(s, k + 16, ss, mx);
-    }
-    // sum and max over the digit warps
     ss = warp_sum(ss);
-    mx = warp_max(mx);
     const uint32_t lane = tid & 31, w = tid >> 5;
-    if (lane == 0) { red[w] = ss; red[kDigitWarps + w] = mx; }
-    digit_sync();
-    float tss = 0.0f, tmx = 0.0f;
-#pragma unroll
-    for (int i = 0; i < kDigitWarps; ++i) { tss += red[i]; tmx = fmaxf(tmx, red[kDigitWarps + i]); }
-    const float f = pro.factor(tss, K);
-    const float m = tmx * f;
-    // m * 2^e in [2^20, 2^21): values round to |v| <= 2^21 (slack for the rounding of m)
-    int e = 0;
-    bad = !isfinite(m);
-    if (m > 0.0f && !bad) {
-        int ex;
-        frexpf(m, &ex);  // m = fr * 2^ex, fr in [0.5, 1)
-        e = 21 - ex;
-    }
-    // v = p * f * 2^e as two products that cannot overflow
-    const float c1 = ldexpf(1.0f, e / 2), c2 = ldexpf(f, e - e / 2);
-#pragma unroll
-    for (int i = 0; i < R; ++i) {
-        const uint32_t idx = tid + kDigitThreads * i;
-        if (idx < items) pack_item(xb, xstride, idx, pa[i], pb[i], c1, c2);
-    }
-    for (uint32_t idx = tid + kDigitThreads * R; idx < items; idx += kDigitThreads) {
-        const uint32_t k = (idx >> 2) * 32 + (idx & 3) * 4;
-        float d0 = 0.0f, d1 = 0.0f;
-        const float4 a = pro.load(s, k, d0, d1), b = pro.load(s, k + 16, d0, d1);
-        pack_item(xb, xstride, idx, a, b, c1, c2);
-    }
+    if (lane == 0) red[w] = ss;
     fence_proxy_async();  // generic-proxy writes -> visible to the tensor cores
     digit_sync();
-    return e;
+    float tss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kDigitWarps; ++i) tss += red[i];
+    return pro.factor(tss, K);
 }
 
 // ---------------------------------------------------------------- epilogues (epilogue warp)
@@ -591,10 +651,10 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
         return;
     }
 
-    // ---------------- warps 1-9: the input vector's digits (every thread gets e and bad)
+    // ---------------- warps 1-9: the input vector's digits (every thread gets the per-vector factor)
     pdl_wait();
-    bool bad = false;
-    const int e = build_digits(pro, K, xb, sh.xstride, redd, threadIdx.x - 32, bad);
+    const float f = block_digits(pro, K, xb, sh.xstride, redd, threadIdx.x - 32);
+    const float* blk = reinterpret_cast<const float*>(xb + blk_off(sh.xstride));
 
     if (warp < kAccWarp0) {
         // ---------------- MMA issue: lane 0 of warp 1+t issues tiles t, t+4 of every stage
@@ -626,7 +686,7 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
     }
 
     if (warp == kFinWarp) {
-        // ---------------- finisher: 2^-e, cross-CTA merge, epilogue
+        // ---------------- finisher: per-vector factor, cross-CTA merge, epilogue
         StreamState est{-INFINITY, 0xFFFFFFFFu};
         bool ok = true;
         uint32_t slot = 0, ph = 0;
@@ -635,7 +695,7 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
             float v[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-                v[i] = bad ? __int_as_float(0x7fc00000) : ldexpf(red[slot][lane + 32 * i], -e);
+                v[i] = red[slot][lane + 32 * i] * f;
             __syncwarp();
             if (lane == 0) mbar_arrive(&red_free[slot]);
             if (++slot == kRedSlots) { slot = 0; ph ^= 1; }
@@ -704,7 +764,7 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
         ++cur_g;
     };
     uint32_t s = 0, ph = 0;
-    acc_stages(u0, u1, NB, nstages, ring, NS, taddr, row, nullptr, mma_done, empty, s, ph, ok, err, acc, cur_g, flush);
+    acc_stages(u0, u1, NB, nstages, ring, NS, taddr, row, blk, mma_done, empty, s, ph, ok, err, acc, cur_g, flush);
     while (cur_g <= g_last) flush();
     tcgen05_fence_before();
     tmem_sync();
@@ -714,9 +774,15 @@ gemv_mma_kernel(UnitW W, MmaShape sh, Pro pro, Epi epi, SplitScratch sp, NextW n
 
 inline uint32_t mma_xstride(uint32_t K) { return ((K / 32) * 48 + 128 + 15) & ~15u; }
 
+// Shared digit area: two digit arrays, then the block factors.
+inline uint32_t mma_digit_bytes(uint32_t K) { return 2 * mma_xstride(K) + (((K / 32) * 4 + 15) & ~15u); }
+
+// Largest K whose digit area fits beside a two-stage ring (220 KB of dynamic shared memory).
+constexpr uint32_t kGemvMaxK = 48384;
+
 inline size_t mma_smem(const MmaShape& sh, uint32_t K) {
     // at least 80 KB, so that no more than two CTAs share an SM's tensor memory
-    const size_t need = (size_t)sh.NS * kStageBytes + 2 * (size_t)mma_xstride(K);
+    const size_t need = (size_t)sh.NS * kStageBytes + mma_digit_bytes(K);
     return need > 80 * 1024 ? need : 80 * 1024;
 }
 
@@ -749,7 +815,7 @@ inline uint32_t mma_ring_bytes(uint32_t K) {
         env_kb = v ? std::atoi(v) : 0;
     }
     if (env_kb >= 36 && env_kb <= 200) return (uint32_t)env_kb * 1024;
-    const uint32_t digits = 2 * mma_xstride(K), two = 2 * kStageBytes;
+    const uint32_t digits = mma_digit_bytes(K), two = 2 * kStageBytes;
     return kMmaCoResidentDyn > digits + two ? kMmaCoResidentDyn - digits : two;
 }
 

@@ -29,6 +29,12 @@ cudaError_t launch_gen_normal(uint64_t seed, uint64_t stream_id, uint64_t offset
                               float* out, cudaStream_t s);
 cudaError_t launch_fill(float* out, uint64_t n, float v, cudaStream_t s);
 
+// Standalone tensor-core GEMV: waits for the call on stream s and turns its
+// bounded-wait flag into BT_ERR_DEVICE_TIMEOUT (clearing flag and tickets).
+int gemv_check_timeout(uint32_t* flag, uint32_t* tickets, size_t ticket_bytes, cudaStream_t s);
+// Sets the no-alloc GEMV's bounded-wait flag on `device` (host-side fault injection for tests).
+int noalloc_inject_timeout(int device);
+
 // Same formula as the CPU oracle (oracle/bt_oracle.c bto_normal_k).
 float normal_k(float sigma);
 uint64_t splitmix64_host(uint64_t z);

@@ -53,7 +53,8 @@ int noalloc_setup(int dev, NoAllocDevice** out) {
         int nsm = 0;
         BT_CUDA_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
         if (nsm <= 0 || (uint32_t)nsm > kNoAllocMaxSMs)
-            return fail(BT_ERR_RUNTIME, "gemv_q8_units_noalloc: device has more SMs than the fixed scratch covers");
+            return fail(BT_ERR_INVALID_ARGUMENT,
+                        "gemv_q8_units_noalloc: device has more SMs than the fixed scratch covers");
         void* p = nullptr;
         BT_CUDA_CHECK(cudaGetSymbolAddress(&p, g_noalloc_scratch));
         d.base = static_cast<unsigned char*>(p);
@@ -65,6 +66,17 @@ int noalloc_setup(int dev, NoAllocDevice** out) {
 }
 
 }  // namespace
+
+int noalloc_inject_timeout(int device) {
+    NoAllocDevice* d = nullptr;
+    int rc = noalloc_setup(device, &d);  // the caller has made `device` current
+    if (rc != BT_OK) return rc;
+    const uint32_t one = 1;
+    BT_CUDA_CHECK(cudaMemcpy(d->base + kNoAllocPartBytes + kNoAllocTickets * sizeof(uint32_t), &one, sizeof(one),
+                             cudaMemcpyHostToDevice));
+    return BT_OK;
+}
+
 }  // namespace bt
 
 using namespace bt;
@@ -72,7 +84,7 @@ using namespace bt;
 extern "C" int bt_cuda_gemv_q8_units_noalloc(const void* units, const float* x, float* y, uint32_t M, uint32_t K,
                                              void* stream) {
     BT_CHECK_ARG(K % 32 == 0 && K > 0, "gemv_q8_units_noalloc: K must be a positive multiple of 32");
-    BT_CHECK_ARG(K <= 48 * 1024, "gemv_q8_units_noalloc: K above 49152 not supported");
+    BT_CHECK_ARG(K <= kGemvMaxK, "gemv_q8_units_noalloc: K above 48384 not supported");
     BT_CHECK_ARG(M <= kNoAllocMaxRows, "gemv_q8_units_noalloc: M above 1048576 rows exceeds the fixed scratch");
     BT_CHECK_ARG(units && x && y, "gemv_q8_units_noalloc: null buffer");
     BT_CHECK_ARG(((uintptr_t)units & 15) == 0 && ((uintptr_t)x & 15) == 0,
@@ -87,10 +99,10 @@ extern "C" int bt_cuda_gemv_q8_units_noalloc(const void* units, const float* x, 
     uint32_t* ticket = reinterpret_cast<uint32_t*>(d->base + kNoAllocPartBytes);
     uint32_t* err = ticket + kNoAllocTickets;
     cudaStream_t s = as_stream(stream);
-    // tickets and the timeout flag start at zero on every call (an earlier call
-    // that timed out may have left them set); the partial sums need no clearing
-    BT_CUDA_CHECK(cudaMemsetAsync(ticket, 0, kNoAllocTicketBytes, s));
+    // the tickets start at zero on every call; the partial sums need no clearing.  The
+    // timeout flag is read (and cleared when set) after the call.
+    BT_CUDA_CHECK(cudaMemsetAsync(ticket, 0, sizeof(uint32_t) * kNoAllocTickets, s));
     const UnitW w{static_cast<const uint8_t*>(units), M, unit_rows(M), K};
     BT_CUDA_CHECK(launch_gemv_mma(w, MProCopy{x}, SEpiStore{y}, SplitScratch{part, ticket}, err, d->nsm, s, false));
-    return BT_OK;
+    return gemv_check_timeout(err, ticket, sizeof(uint32_t) * kNoAllocTickets, s);
 }

@@ -52,6 +52,22 @@ static int gemv_workspace(int dev, GemvWorkspace** out) {
     return BT_OK;
 }
 
+// After a standalone tensor-core GEMV on stream s: waits for it and reads its
+// bounded-wait flag.  A set flag means a wait inside the kernel gave up after
+// its 2 s limit, so y is not valid; the flag and the arrival tickets (which an
+// interrupted call may leave mid-count) are then cleared for the next call and
+// BT_ERR_DEVICE_TIMEOUT is returned.
+int gemv_check_timeout(uint32_t* flag, uint32_t* tickets, size_t ticket_bytes, cudaStream_t s) {
+    uint32_t h = 0;
+    BT_CUDA_CHECK(cudaStreamSynchronize(s));
+    BT_CUDA_CHECK(cudaMemcpy(&h, flag, sizeof(h), cudaMemcpyDeviceToHost));
+    if (h == 0) return BT_OK;
+    BT_CUDA_CHECK(cudaMemsetAsync(tickets, 0, ticket_bytes, s));
+    BT_CUDA_CHECK(cudaMemsetAsync(flag, 0, sizeof(uint32_t), s));
+    BT_CUDA_CHECK(cudaStreamSynchronize(s));
+    return fail(BT_ERR_DEVICE_TIMEOUT, "gemv_q8_units: a device wait timed out; the output is not valid");
+}
+
 // cpu_ref::rmsnorm (cpu_ref.hpp:11-28): one CTA per row.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ in, const float* __restrict__ w,
                                                       float* __restrict__ out, uint32_t dim, float eps) {
@@ -363,7 +379,7 @@ int bt_cuda_matvec_q8_0(const void* W_blocks, const float* X, float* Y, uint32_t
 
 int bt_cuda_gemv_q8_units(const void* units, const float* x, float* y, uint32_t M, uint32_t K, void* stream) {
     BT_CHECK_ARG(K % 32 == 0 && K > 0, "gemv_q8_units: K must be a positive multiple of 32");
-    BT_CHECK_ARG(K <= 48 * 1024, "gemv_q8_units: K above 49152 not supported");
+    BT_CHECK_ARG(K <= kGemvMaxK, "gemv_q8_units: K above 48384 not supported");
     BT_CHECK_ARG(units && x && y, "gemv_q8_units: null buffer");
     BT_CHECK_ARG(((uintptr_t)units & 15) == 0 && ((uintptr_t)x & 15) == 0,
                  "gemv_q8_units: units and x must be 16-byte aligned");
@@ -375,9 +391,30 @@ int bt_cuda_gemv_q8_units(const void* units, const float* x, float* y, uint32_t 
     int rc = gemv_workspace(dev, &ws);
     if (rc != BT_OK) return rc;
     const UnitW w{static_cast<const uint8_t*>(units), M, unit_rows(M), K};
+    cudaStream_t s = as_stream(stream);
     BT_CUDA_CHECK(launch_gemv_mma(w, MProCopy{x}, SEpiStore{y}, SplitScratch{ws->part, ws->ticket},
-                                  ws->ticket + kWsTickets, ws->nsm, as_stream(stream), false));
-    return BT_OK;
+                                  ws->ticket + kWsTickets, ws->nsm, s, false));
+    return gemv_check_timeout(ws->ticket + kWsTickets, ws->ticket, sizeof(uint32_t) * kWsTickets, s);
+}
+
+int bt_cuda_gemv_inject_timeout(int device, int noalloc) {
+    int prev = 0;
+    BT_CUDA_CHECK(cudaGetDevice(&prev));
+    BT_CUDA_CHECK(cudaSetDevice(device));
+    int rc = BT_OK;
+    if (noalloc) {
+        rc = noalloc_inject_timeout(device);
+    } else {
+        GemvWorkspace* ws = nullptr;
+        rc = gemv_workspace(device, &ws);
+        const uint32_t one = 1;
+        if (rc == BT_OK) {
+            const cudaError_t ce = cudaMemcpy(ws->ticket + kWsTickets, &one, sizeof(one), cudaMemcpyHostToDevice);
+            if (ce != cudaSuccess) rc = fail(BT_ERR_CUDA, std::string("gemv_inject_timeout: ") + cudaGetErrorString(ce));
+        }
+    }
+    cudaSetDevice(prev);
+    return rc;
 }
 
 int bt_cuda_gemv_q8(const int8_t* qs, const float* scales, const float* X, float* Y, uint32_t M, uint32_t K,

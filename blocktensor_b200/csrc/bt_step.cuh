@@ -73,6 +73,24 @@ struct StepArgs {
     uint32_t tp_rank, tp_world;
     float eps, scale;
     uint32_t NS, xstride, tmem_cols, scratch_off;
+    // L2 prefetch of upcoming weight stages while the consumers are held up (0: off), and
+    // kStepFlag* options
+    uint32_t pf_stages, flags;
+    // per-phase device timestamps (null: off): [P][G][kTraceSlots] of %globaltimer
+    uint64_t* trace;
+};
+
+constexpr uint32_t kStepFlagEvictFirst = 1;  // ring copies mark their L2 lines evict-first
+
+// Timestamps of the trace (per phase and CTA), in %globaltimer nanoseconds.
+enum : uint32_t {
+    kTrStart = 0,     // consumers pass the phase's counter wait
+    kTrDigits = 1,    // the input's digits are in shared memory
+    kTrFirstAcc = 2,  // the finisher receives its first row tile's sums
+    kTrEnd = 3,       // the CTA's writes of the phase are done (its counter release)
+    kTrCopy0 = 4,     // the producer issues the phase's first ring copy
+    kTrCopy1 = 5,     // ... and its last
+    kTraceSlots = 8
 };
 
 constexpr uint32_t kTpMaxWorld = 8;  // GPUs of one tensor parallel group
@@ -114,6 +132,48 @@ __device__ __forceinline__ Geo phase_geo(const StepMat& m, uint32_t c, uint32_t 
     return r;
 }
 
+// Position of a CTA in the stream of its weight stages over the GEMV phases of
+// the step (the producer copies them in this order, and prefetches ahead of
+// the copies in the same order).
+struct StageCursor {
+    uint32_t p, j, nst, u0, u1;
+    const uint8_t* units;
+};
+
+// Moves k to stage 0 of the first phase >= k.p that has stages for CTA c (k.p = P: the end).
+__device__ __forceinline__ void cursor_settle(StageCursor& k, const StepArgs& a, uint32_t P, uint32_t c, uint32_t G) {
+    for (; k.p < P; ++k.p) {
+        if (phase_kind(k.p, a.L) == kPhAttn) continue;
+        const StepMat mt = phase_mat(a, k.p);
+        const Geo gm = phase_geo(mt, c, G);
+        if (gm.nstages) {
+            k.j = 0;
+            k.nst = gm.nstages;
+            k.u0 = gm.u0;
+            k.u1 = gm.u1;
+            k.units = mt.units;
+            return;
+        }
+    }
+}
+
+__device__ __forceinline__ void cursor_next(StageCursor& k, const StepArgs& a, uint32_t P, uint32_t c, uint32_t G) {
+    if (++k.j < k.nst) return;
+    ++k.p;
+    cursor_settle(k, a, P, c, G);
+}
+
+// Source and size of the stage at k.
+__device__ __forceinline__ const uint8_t* cursor_src(const StageCursor& k, uint32_t& bytes) {
+    const uint32_t ub = k.u0 + k.j * kStageTiles;
+    bytes = min(kStageTiles, k.u1 - ub) * kTileBytes;
+    return k.units + (size_t)ub * kTileBytes;
+}
+
+__device__ __forceinline__ void trace_at(const StepArgs& a, uint32_t p, uint32_t slot) {
+    if (a.trace) a.trace[((size_t)p * gridDim.x + blockIdx.x) * kTraceSlots + slot] = global_ns();
+}
+
 __device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
 // Atomic add with acquire and release semantics at gpu scope; returns the old value.
@@ -135,9 +195,9 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
 }
 
 // Prologue of any GEMV of the step: RMSNorm with weight w (kernels/cpu_ref.hpp:11-28)
-// or, when w is null, a plain copy; the element loads are step_x / step_p below.
-// With `embed` the source is the embedding row of the current token and CTA 0
-// also writes it to x_out.  Activations are read through L2.
+// or, when w is null, a plain copy.  With `embed` the source is the embedding
+// row of the current token and CTA 0 also writes it to x_out.  Activations are
+// read through L2.
 struct MProStep {
     const float* src;
     const float* w;
@@ -149,29 +209,24 @@ struct MProStep {
     __device__ float factor(float ss, uint32_t K) const {
         return w ? __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps))) : 1.0f;
     }
-};
-
-// Elements of a GEMV phase's input: x (embedding row or activations through L2),
-// p = x * w with the RMSNorm weight w (or p = x), and the sums the norm needs.
-__device__ __forceinline__ float4 step_x(const MProStep& pro, const float* s, uint32_t k) {
-    return pro.embed ? *reinterpret_cast<const float4*>(s + k) : ldcg4(s + k);
-}
-
-__device__ __forceinline__ float4 step_p(const MProStep& pro, const float4& v, const float4& g, uint32_t k, float& ss,
-                                         float& mx) {
-    if (!pro.w) {
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-        return v;
+    // x (embedding row, or activations through L2), p = x * w (or p = x), and the sums the norm needs
+    __device__ float4 load(const float* s, uint32_t k, float& ss, float& mx) const {
+        const float4 v = embed ? *reinterpret_cast<const float4*>(s + k) : ldcg4(s + k);
+        if (!w) {
+            amax4(mx, v);
+            return v;
+        }
+        const float4 g = *reinterpret_cast<const float4*>(w + k);
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+        if (embed && blockIdx.x == 0) *reinterpret_cast<float4*>(x_out + k) = v;
+        const float4 p = make_float4(v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w);
+        amax4(mx, p);
+        return p;
     }
-    ss = fmaf(v.x, v.x, ss);
-    ss = fmaf(v.y, v.y, ss);
-    ss = fmaf(v.z, v.z, ss);
-    ss = fmaf(v.w, v.w, ss);
-    if (pro.embed && blockIdx.x == 0) *reinterpret_cast<float4*>(pro.x_out + k) = v;
-    const float4 p = make_float4(v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w);
-    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(p.x), fabsf(p.y)), fmaxf(fabsf(p.z), fabsf(p.w))));
-    return p;
-}
+};
 
 // Waits (one thread) until cnt reaches target; bounded, and no wait at all
 // once an earlier wait of the step has timed out (*err set).
@@ -199,106 +254,9 @@ __device__ __forceinline__ void wait_count(const uint32_t* cnt, uint32_t target,
 // the next phase's image to global memory; the next phase fetches it with
 // bulk copies.
 
-__device__ __forceinline__ uint32_t blk_off(uint32_t xstride) { return 2 * xstride; }
-
-__device__ __forceinline__ int block_exponent(float am, bool& finite) {
-    finite = isfinite(am);
-    int e = 0;
-    if (am > 0.0f && finite) {
-        int ex;  // am = fr * 2^ex, fr in [0.5, 1)
-        if (am >= 1.17549435e-38f)
-            ex = ((__float_as_int(am) >> 23) & 255) - 126;
-        else
-            frexpf(am, &ex);
-        e = 21 - ex;
-        if (e > 149) e = 149;  // 2^-e stays representable
-    }
-    return e;
-}
-
-// 2^k for |k| <= 126, exactly.
-__device__ __forceinline__ float pow2i(int k) { return __int_as_float((127 + k) << 23); }
-
-// 2^-e for the block exponents above (subnormal below 2^-126).
-__device__ __forceinline__ float pow2neg(int e) { return e <= 126 ? pow2i(-e) : ldexpf(1.0f, -e); }
-
-// round(p * 2^e) for |p * 2^e| <= 2^21 (round half to even, as cvt.rni).
-__device__ __forceinline__ int scaled_round(float p, int e) {
-    const float t = __fmul_rn(__fmul_rn(p, pow2i(e / 2)), pow2i(e - e / 2));
-    return __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
-}
-
-// One warp, lane i holding element i of block b (warp-uniform call).  The
-// block's max |p| is one redux.sync on the bit patterns (monotonic for
-// non-negative floats; an inf or NaN anywhere makes the block's scale NaN, so
-// it propagates to every output as in fp32 arithmetic); each lane packs its
-// three digit bytes into one word and three shuffles bring the next lanes'
-// words for the 4-element digit words of lanes 0, 4, ... .
+// Digits of block b of the shared-area layout (see warp_digits).
 __device__ __forceinline__ void warp_block_digits(uint8_t* img, uint32_t xstride, uint32_t b, float p, uint32_t lane) {
-    const float am = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(p))));
-    bool finite;
-    const int e = block_exponent(am, finite);
-    const int v = finite ? scaled_round(p, e) : 0;
-    int hi, mid, lo;
-    digits3(v, hi, mid, lo);
-    const uint32_t w0 = ((uint32_t)hi & 255u) | (((uint32_t)mid & 255u) << 8) | (((uint32_t)lo & 255u) << 16);
-    const uint32_t w1 = __shfl_down_sync(0xffffffffu, w0, 1);
-    const uint32_t w2 = __shfl_down_sync(0xffffffffu, w0, 2);
-    const uint32_t w3 = __shfl_down_sync(0xffffffffu, w0, 3);
-    if ((lane & 3) == 0) {
-        // digit d of elements lane .. lane+3: byte d of w0, w1, w2, w3
-        const uint32_t a01 = __byte_perm(w0, w1, 0x5140), a23 = __byte_perm(w2, w3, 0x5140);  // hi, mid bytes
-        const uint32_t b01 = __byte_perm(w0, w1, 0x0062), b23 = __byte_perm(w2, w3, 0x0062);  // lo bytes
-        uint8_t* q = img + (lane >> 4) * xstride + b * 48 + (lane & 15);
-        *reinterpret_cast<uint32_t*>(q) = __byte_perm(a01, a23, 0x5410);        // hi
-        *reinterpret_cast<uint32_t*>(q + 16) = __byte_perm(a01, a23, 0x7632);   // mid
-        *reinterpret_cast<uint32_t*>(q + 32) = __byte_perm(b01, b23, 0x5410);   // lo
-    }
-    if (lane == 0)
-        *reinterpret_cast<float*>(img + blk_off(xstride) + 4 * b) = finite ? pow2neg(e) : __int_as_float(0x7fc00000);
-}
-
-// A CTA builds the shared digit area of a whole input vector itself (the
-// embedding row of layer 0, or an input no finisher writes).  Digit threads
-// only; returns the RMSNorm factor (1 without a norm weight).
-__device__ float local_digits(const MProStep& pro, uint32_t K, uint8_t* xb, uint32_t xstride, float* red, uint32_t tid) {
-    const float* s = pro.base(K);
-    const uint32_t items = K >> 3;
-    const float4 one = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
-    float ss = 0.0f;
-    for (uint32_t i0 = 0; i0 < items; i0 += kDigitThreads) {  // same trip count in every thread (shuffles below)
-        const uint32_t idx = i0 + tid;
-        const bool valid = idx < items;
-        const uint32_t k = (idx >> 2) * 32 + (idx & 3) * 4;
-        float4 pa = make_float4(0.f, 0.f, 0.f, 0.f), pb = pa;
-        float mx = 0.0f;
-        if (valid) {
-            const float4 ga = pro.w ? *reinterpret_cast<const float4*>(pro.w + k) : one;
-            const float4 gb = pro.w ? *reinterpret_cast<const float4*>(pro.w + k + 16) : one;
-            pa = step_p(pro, step_x(pro, s, k), ga, k, ss, mx);
-            pb = step_p(pro, step_x(pro, s, k + 16), gb, k + 16, ss, mx);
-        }
-        // the 4 items of a block are 4 consecutive lanes
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        bool finite;
-        const int e = block_exponent(mx, finite);
-        if (valid) {
-            pack_item(xb, xstride, idx, pa, pb, pow2i(e / 2), pow2i(e - e / 2));
-            if ((idx & 3) == 0)
-                *reinterpret_cast<float*>(xb + blk_off(xstride) + 4 * (idx >> 2)) =
-                    finite ? pow2neg(e) : __int_as_float(0x7fc00000);
-        }
-    }
-    ss = warp_sum(ss);
-    const uint32_t lane = tid & 31, w = tid >> 5;
-    if (lane == 0) red[w] = ss;
-    fence_proxy_async();  // generic-proxy writes -> visible to the tensor cores
-    digit_sync();
-    float tss = 0.0f;
-#pragma unroll
-    for (int i = 0; i < kDigitWarps; ++i) tss += red[i];
-    return pro.factor(tss, K);
+    warp_digits(img + b * 48, xstride, reinterpret_cast<float*>(img + blk_off(xstride)) + b, p, lane);
 }
 
 // RMSNorm factor of a phase fed by a digit image: 1/sqrt(sum of the row-tile
@@ -596,22 +554,62 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
         // ---------------- producer: every GEMV of the step, back to back
         if (lane == 0) {
             uint32_t issued = 0, s = 0, ph = 0;
+            uint32_t s_last = 0, ph_last = 0;  // ring slot and barrier parity of the latest copy
             bool ok = true;
-            for (uint32_t p = 0; p < P && ok; ++p) {
-                if (phase_kind(p, a.L) == kPhAttn) continue;
-                const StepMat mt = phase_mat(a, p);
-                const Geo gm = phase_geo(mt, c, G);
-                for (uint32_t j = 0; j < gm.nstages; ++j) {
-                    if (issued >= NS && !(ok = mbar_wait(&empty[s], ph ^ 1, err))) break;
-                    const uint32_t ub = gm.u0 + j * kStageTiles;
-                    const uint32_t n = min(kStageTiles, gm.u1 - ub);
-                    mbar_expect_tx(&full[s], n * kTileBytes);
-                    bulk_g2s(ring + (size_t)s * kStageBytes, mt.units + (size_t)ub * kTileBytes, n * kTileBytes,
-                             &full[s]);
-                    ++issued;
-                    if (++s == NS) { s = 0; ph ^= 1; }
+            StageCursor cp{0, 0, 0, 0, 0, nullptr};
+            cursor_settle(cp, a, P, c, G);
+            // L2 prefetch: pf runs pf_ahead stages in front of the copies (pf == cp when 0)
+            StageCursor pf = cp;
+            uint32_t pf_ahead = 0;
+            const uint64_t pol = policy_evict_first();
+            const bool hint = (a.flags & kStepFlagEvictFirst) != 0;
+            uint32_t p_traced = 0xFFFFFFFFu;
+            while (cp.p < P && ok) {
+                if (issued >= NS) {
+                    // slot s is free once the accumulators release it.  While it is not, and every
+                    // copy issued so far has landed, the consumers are held up (a phase boundary,
+                    // attention) and this CTA's HBM stream is idle: bring upcoming stages into L2.
+                    const uint64_t t0 = global_ns();
+                    while (!mbar_try_wait(&empty[s], ph ^ 1)) {
+                        if (pf_ahead < a.pf_stages && pf.p < P && mbar_try_wait(&full[s_last], ph_last)) {
+                            while (pf_ahead < a.pf_stages && pf.p < P) {
+                                uint32_t nb;
+                                const uint8_t* src = cursor_src(pf, nb);
+                                bulk_prefetch_l2(src, nb);
+                                ++pf_ahead;
+                                cursor_next(pf, a, P, c, G);
+                            }
+                        }
+                        if (mbar_try_wait_sleep(&empty[s], ph ^ 1, pf_ahead < a.pf_stages ? 1000u : 100000u)) break;
+                        if (global_ns() - t0 > kWaitNs) {
+                            atomicExch(err, 1u);
+                            ok = false;
+                            break;
+                        }
+                    }
+                    if (!ok) break;
                 }
+                if (a.trace && cp.p != p_traced) {
+                    if (p_traced != 0xFFFFFFFFu) trace_at(a, p_traced, kTrCopy1);
+                    trace_at(a, cp.p, kTrCopy0);
+                    p_traced = cp.p;
+                }
+                uint32_t nb;
+                const uint8_t* src = cursor_src(cp, nb);
+                mbar_expect_tx(&full[s], nb);
+                if (hint)
+                    bulk_g2s_hint(ring + (size_t)s * kStageBytes, src, nb, &full[s], pol);
+                else
+                    bulk_g2s(ring + (size_t)s * kStageBytes, src, nb, &full[s]);
+                s_last = s;
+                ph_last = ph;
+                ++issued;
+                cursor_next(cp, a, P, c, G);
+                if (pf_ahead > 0) --pf_ahead;
+                else pf = cp;
+                if (++s == NS) { s = 0; ph ^= 1; }
             }
+            if (a.trace && p_traced != 0xFFFFFFFFu) trace_at(a, p_traced, kTrCopy1);
             const uint32_t first = issued > NS ? issued - NS : 0;
             for (uint32_t j = first; j < issued; ++j) mbar_wait(&full[j % NS], (j / NS) & 1, nullptr);
         }
@@ -624,6 +622,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
     const uint32_t target = G * (epoch + 1);
     const uint32_t pos = a.st->pos;  // changed only by the head phase's last CTA, at the very end
     const uint32_t launch = a.am_ticket[1];  // step launches of the engine so far (bumped at the very end)
+    // Tag of this launch's phase-p partials: ((launch mod (2^22 - 1)) + 1) << 10 | p.  Its launch
+    // bits are never 0 (zeroed buffers never match) and consecutive launches never share a tag,
+    // also across the wrap of the 32-bit launch count, so a slot still holding the previous
+    // launch's words is never taken for this launch's.
+    const uint32_t tag_base = ((launch % 0x3FFFFFu) + 1u) << 10;
     bool ok = true;
     // per-role pipeline state, carried across phases
     uint32_t rs = 0, rph = 0;              // ring slot (issuers, accumulators)
@@ -638,13 +641,17 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
             if (tid == 0) wait_count(a.cnt + (p - 1), target, err);  // acquire
             digit_sync();
         }
+        if (tid == 0) trace_at(a, p, kTrStart);
         if (kind == kPhQKV && tid == 32 * 8) prefetch_attn_rows<KVT>(a, l);  // the finisher warp, before its first group
         uint8_t* img_next = a.dimg[(p + 1) & 1];
         float* ssp_next = a.ssp[(p + 1) & 1];
         if (kind == kPhAttn) {
-            attn_phase<NV, GQM, KVT>(a, l, xb, tid, a.hd % 32 == 0 ? img_next : nullptr, ((launch + 1) << 10) | p, ok);
+            attn_phase<NV, GQM, KVT>(a, l, xb, tid, a.hd % 32 == 0 ? img_next : nullptr, tag_base | p, ok);
             // the CTA's writes are ordered before the release by the barrier that ends the item
-            if (tid == 0) red_add_release_gpu(a.cnt + p, 1u);
+            if (tid == 0) {
+                trace_at(a, p, kTrEnd);
+                red_add_release_gpu(a.cnt + p, 1u);
+            }
             continue;
         }
         const Geo gm = phase_geo(mt, c, G);
@@ -672,8 +679,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                 pro.w = a.layers[l].attn_norm;
                 pro.embed = a.embed;  // layer 0
             }
-            inv = local_digits(pro, mt.K, xb, a.xstride, redd, tid);
+            inv = block_digits(pro, mt.K, xb, a.xstride, redd, tid);  // the image an input no finisher writes
         }
+        if (tid == 0) trace_at(a, p, kTrDigits);
         const float* blk = reinterpret_cast<const float*>(xb + blk_off(a.xstride));
 
         if (warp < kAccWarp0) {
@@ -711,8 +719,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                                  : kind == kPhDown ? (l + 1 < a.L ? a.layers[l + 1].attn_norm : a.out_norm)
                                                    : nullptr;
             const uint32_t NBn = kind == kPhGU ? a.F / kTileK : a.D / kTileK;  // blocks of the next input
-            // tag of this launch's phase-p partials: never 0, never a value of another launch or phase
-            const uint32_t tag = ((launch + 1) << 10) | p;
+            const uint32_t tag = tag_base | p;
             const uint32_t half = a.hd >> 1;
             KVT* kl = reinterpret_cast<KVT*>(a.kc) + (size_t)l * a.KVH * a.max_seq * a.hd;
             KVT* vl = reinterpret_cast<KVT*>(a.vc) + (size_t)l * a.KVH * a.max_seq * a.hd;
@@ -737,6 +744,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                     }
                 }
                 if (ok) ok = mbar_wait(&red_full[qs], qph, err);
+                if (g == gm.g_first && lane == 0) trace_at(a, p, kTrFirstAcc);
                 float v[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) v[i] = red[qs][lane + 32 * i] * inv;
@@ -911,6 +919,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                 }
                 __syncwarp();
             }
+            if (lane == 0) trace_at(a, p, kTrEnd);
             if (kind == kPhHead) {
                 EpiLogits lg{a.logits, a.am_val, a.am_idx, a.am_ticket, a.st, a.tok_hist, a.max_seq, true};
                 lg.v0 = a.v0;

@@ -84,9 +84,11 @@ SIGNATURES = {
     "bt_cuda_matvec_q8_0": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp]),
     "bt_cuda_repack_q8_0": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp]),
     "bt_cuda_gemv_q8": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp]),
+    "bt_cuda_gemm_q8_units": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32, _vp]),
     "bt_cuda_pack_q8_units": (_i32, [_vp, _vp, _u32, _u32, _vp]),
     "bt_cuda_gemv_q8_units": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp]),
     "bt_cuda_gemv_q8_units_noalloc": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp]),
+    "bt_cuda_gemv_inject_timeout": (_i32, [_i32, _i32]),
     "bt_cuda_rmsnorm": (_i32, [_vp, _vp, _vp, _u32, _u32, _f32, _vp]),
     "bt_cuda_rope": (_i32, [_vp, _vp, _u32, _u32, _u32, _u32, _f32, _vp]),
     "bt_cuda_softmax": (_i32, [_vp, _vp, _u32, _u32, _vp]),
@@ -101,8 +103,12 @@ SIGNATURES = {
     "bt_kv_read_layer": (_i32, [_vp, _u32, _vp, _vp]),
     "bt_engine_forward_token": (_i32, [_vp, _vp, _u32, _u32, _vp, _vp]),
     "bt_engine_decode": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32, _vp]),
+    "bt_engine_prefill": (_i32, [_vp, _vp, _vp, _u32, _u32]),
+    "bt_kv_read_tokens": (_i32, [_vp, _u32, _u32, _vp]),
     "bt_engine_set_taps": (_i32, [_vp, _i32]),
     "bt_engine_read_taps": (_i32, [_vp, _vp]),
+    "bt_engine_set_trace": (_i32, [_vp, _i32]),
+    "bt_engine_read_trace": (_i32, [_vp, _vp, _u64]),
     "bt_engine_tp_handle": (_i32, [_vp, _vp]),
     "bt_engine_tp_connect": (_i32, [_vp, _vp]),
     "bt_engine_begin": (_i32, [_vp, _vp, _vp, _u32, _u32]),

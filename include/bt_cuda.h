@@ -156,10 +156,13 @@ BT_API int bt_cuda_pack_q8_units(const void* W_blocks, void* units, uint32_t M, 
 
 /* y[m] = sum_k W[m][k] x[k] on the tile layout: quantization::matvec_q8_0
  * (quant_types.cpp:101-121) on the tensor cores (tcgen05 int8 MMA: exact block
- * dot products, x as 22-bit fixed point, fp32 block accumulation), split evenly
- * over all SMs.  units and x must be 16-byte aligned; M <= 1048576.  Scratch for
- * row tiles split between CTAs comes from a per-device workspace the library
- * allocates on the first call. */
+ * dot products, every 32-element block of x in 22-bit fixed point with its own
+ * exponent, fp32 block accumulation), split evenly over all SMs.  units and x
+ * must be 16-byte aligned; M <= 1048576, K <= 48384.  Scratch for row tiles
+ * split between CTAs comes from a per-device workspace the library allocates
+ * on the first call.  Returns once the GEMV has finished on `stream` (like the
+ * reference's synchronous matvec): BT_ERR_DEVICE_TIMEOUT when a wait inside
+ * the kernel gave up after its 2 s limit (y is then not valid). */
 BT_API int bt_cuda_gemv_q8_units(const void* units, const float* x, float* y, uint32_t M, uint32_t K,
                                  void* stream);
 
@@ -172,15 +175,37 @@ BT_API int bt_cuda_gemv_q8_units(const void* units, const float* x, float* y, ui
  * scratch (partial sums of row groups split between CTAs, arrival tickets, a
  * timeout flag) is a fixed 288 KB device array inside the library, held by
  * every GPU that loads the library until the process exits.  Limits: M <=
- * 1048576 rows, K <= 49152, at most 256 SMs; larger sizes return
+ * 1048576 rows, K <= 48384, at most 256 SMs; larger sizes return
  * BT_ERR_INVALID_ARGUMENT.  The first call on a device looks up the array's
  * device address (cudaGetSymbolAddress, with that device current); make that
  * first call before any stream capture.  Every call on a device shares the one
  * array and each call clears its tickets first, so calls that overlap on the
  * GPU (concurrent streams) race and must be serialised by the caller.  Same
- * inputs, outputs, alignment and arithmetic as bt_cuda_gemv_q8_units. */
+ * inputs, outputs, alignment, arithmetic and completion (returns once the GEMV
+ * has finished; BT_ERR_DEVICE_TIMEOUT when a device wait gave up) as
+ * bt_cuda_gemv_q8_units. */
 BT_API int bt_cuda_gemv_q8_units_noalloc(const void* units, const float* x, float* y, uint32_t M, uint32_t K,
                                          void* stream);
+
+/* Fault injection on the host, for tests of the standalone GEMVs' timeout
+ * reporting (no counterpart in the reference): sets the bounded-wait flag of
+ * bt_cuda_gemv_q8_units (noalloc = 0) or of bt_cuda_gemv_q8_units_noalloc
+ * (noalloc = 1) on `device`, as an expired device wait would, so that the next
+ * call of that entry point returns BT_ERR_DEVICE_TIMEOUT and clears it.  No
+ * GPU fault, no hang. */
+BT_API int bt_cuda_gemv_inject_timeout(int device, int noalloc);
+
+/* Y[t][m] = sum_k W[m][k] X[t][k] for T token rows on the tile layout: the
+ * reference's matvec_q8_0 (quant_types.cpp:101-121) for every row of X, as one
+ * tensor-core GEMM (tcgen05 int8 MMA over 32-token groups: exact block dot
+ * products of every token's 22-bit per-block fixed point digits, fp32 block
+ * accumulation in the reference's block order).  This is the contraction of
+ * prompt prefill and batched decode, exposed for its parity tests.  X [T][K]
+ * and Y [T][M] are fp32 row-major; units and X 16-byte aligned.  Returns once
+ * finished on `stream`; scratch (the digit image of X) is allocated
+ * stream-ordered per call.  BT_ERR_DEVICE_TIMEOUT when a device wait gave up. */
+BT_API int bt_cuda_gemm_q8_units(const void* units, const float* X, float* Y, uint32_t M, uint32_t K, uint32_t T,
+                                 void* stream);
 
 /* Batched int8 GEMV on the device layout: Y[b][m] = sum_k W[m][k] X[b][k],
  * b < B, for the dequant-GEMV microbenchmark.  B = 1 is the
@@ -256,11 +281,40 @@ BT_API int bt_engine_forward_token(bt_engine* e, bt_kv* kv, uint32_t token, uint
 BT_API int bt_engine_decode(bt_engine* e, bt_kv* kv, const uint32_t* prompt, uint32_t n_prompt,
                      uint32_t pos0, uint32_t n_gen, uint32_t* tokens_out);
 
+/* Prompt prefill: the batched form of the reference's prompt loop
+ * (benchmarks/bench_runner.cpp:107-109, tools/bt_infer.cpp:116-125).  The
+ * positions pos0 .. pos0 + n_prompt - 2 run through every layer together as
+ * tensor-core GEMMs (chunks of up to 512 tokens) with causal attention over the
+ * cache, filling their K/V rows; the sequence is then left as
+ * bt_engine_begin(prompt, n_prompt, pos0) leaves it after n_prompt - 1 steps:
+ * the next bt_engine_steps step processes prompt[n_prompt - 1] at position
+ * pos0 + n_prompt - 1 (its logits and greedy token come from the decode step)
+ * and decoding continues greedily.  Needs the persistent step kernel and no
+ * tensor parallelism.  Errors as bt_engine_begin; BT_ERR_DEVICE_TIMEOUT when a
+ * device wait gave up. */
+BT_API int bt_engine_prefill(bt_engine* e, bt_kv* kv, const uint32_t* prompt, uint32_t n_prompt, uint32_t pos0);
+/* Token consumed at positions pos0 .. pos0 + n - 1 (the prompt, then the
+ * greedy tokens; entry max_seq is the argmax after the last position). */
+BT_API int bt_kv_read_tokens(bt_kv* kv, uint32_t pos0, uint32_t n, uint32_t* out);
+
 /* Per-layer residual-stream taps: when enabled, every subsequent step records
  * x after each layer; bt_engine_read_taps copies [num_layers][dim] fp32 of the
  * last step to host. */
 BT_API int bt_engine_set_taps(bt_engine* e, int enable);
 BT_API int bt_engine_read_taps(bt_engine* e, float* taps);
+
+/* Per-phase device timestamps of the persistent step kernel, for latency
+ * analysis (no counterpart in the reference).  When enabled, every subsequent
+ * step records, for every phase p (5 per layer, then the head) and CTA c, the
+ * %globaltimer nanoseconds of: [0] the consumers passing the phase's counter
+ * wait, [1] the input digits ready in shared memory, [2] the first row tile's
+ * sums reaching the finisher, [3] the CTA's last write of the phase, [4] and
+ * [5] the producer issuing the phase's first and last weight copy; slots 6-7
+ * are unused.  bt_engine_read_trace copies the last step's
+ * [5 L + 1][SMs][8] words (n_words must equal that count).  The recording
+ * costs a few stores per phase; off by default. */
+BT_API int bt_engine_set_trace(bt_engine* e, int enable);
+BT_API int bt_engine_read_trace(bt_engine* e, uint64_t* out, uint64_t n_words);
 
 /* Device-side timing hooks for benchmarks: run n decode steps on `stream`
  * with no host synchronisation; the device state (position, current token)

@@ -18,6 +18,13 @@ sources (``make -C oracle``):
   seed 0) with a short prompt: greedy tokens with fp32 KV (checked against
   the reference engine for the first steps) and with fp16 KV (restatement),
   top-2 logit margins, logits of one step and residual taps of a few layers.
+* llama7b_c2_p512.npz -- the same model at the benchmarked configuration: a
+  512-token prompt and 32 greedy tokens (contexts up to 544), fp16 and fp32 KV,
+  with logits and taps of a few layers at the last prompt position and at the
+  last generated position.  The restatement runs multithreaded (rows of each
+  matvec split between threads, every row summed in the reference's order, so
+  the results do not depend on the thread count) and is checked against the
+  reference engine on the first positions.
 """
 from __future__ import annotations
 
@@ -199,11 +206,59 @@ def llama7b(ref: O.RefLib, n_prompt: int = 8, n_gen: int = 32, ref_steps: int = 
     return out
 
 
+def llama7b_long(ref: O.RefLib, n_prompt: int = 512, n_gen: int = 32, ref_steps: int = 2):
+    cfg = O.make_config(32000, 4096, 11008, 32, 32, 32, 128, 1024)
+    t0 = time.time()
+    m = O.Model(cfg, seed=0)
+    print(f"  7B model generated in {time.time() - t0:.1f} s", flush=True)
+    prompt = O.gen_tokens(0, O.STREAM_PROMPT, n_prompt, cfg.vocab_size)
+    max_seq = n_prompt + n_gen + 1
+    layers = [0, 1, 15, 31]
+    out = dict(config=np.frombuffer(bytes(cfg), np.uint8), prompt=prompt, tap_layers=np.array(layers, np.int32))
+    eng = O.RefEngine(ref, m, kv_max_seq=max_seq) if ref_steps else None
+    for name, fp16 in (("kv16", True), ("kv32", False)):
+        kv = O.KV(cfg, max_seq, fp16=fp16)
+        toks = [int(prompt[0])]
+        margins, top = [], []
+        t0 = time.time()
+        for p in range(n_prompt + n_gen):
+            lo, taps = O.forward_token(m, kv, toks[p], p, want_taps=True)
+            if eng is not None and not fp16 and p < ref_steps:
+                lr = eng.forward(toks[p], p)
+                assert np.array_equal(lr, lo), f"oracle differs from reference engine at 7B pos {p}"
+            srt = np.argsort(lo)[::-1]
+            margins.append(lo[srt[0]] - lo[srt[1]])
+            top.append(srt[:8].astype(np.uint32))
+            for tag, at in (("last_prompt", n_prompt - 1), ("last_gen", n_prompt + n_gen - 1)):
+                if p == at:
+                    out[f"{name}_logits_{tag}"] = lo
+                    out[f"{name}_taps_{tag}"] = taps[layers]
+                    out[f"{name}_tap_norms_{tag}"] = np.linalg.norm(taps, axis=1).astype(np.float32)
+            nxt = int(prompt[p + 1]) if p + 1 < n_prompt else int(srt[0])
+            toks.append(nxt)
+            if p % 64 == 63:
+                print(f"  7B {name}: {p + 1} steps, {time.time() - t0:.0f} s", flush=True)
+        out[f"{name}_tokens"] = np.array(toks, np.uint32)
+        out[f"{name}_margins"] = np.array(margins, np.float32)
+        out[f"{name}_top8"] = np.stack(top)
+        kv.close()
+    if eng is not None:
+        eng.close()
+    m.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--skip-7b", action="store_true")
+    ap.add_argument("--only-7b-long", action="store_true",
+                    help="write only llama7b_c2_p512.npz (the benchmarked 512-token configuration)")
     a = ap.parse_args()
     ref = O.RefLib()
+    if a.only_7b_long:
+        np.savez_compressed(os.path.join(HERE, "llama7b_c2_p512.npz"), **llama7b_long(ref))
+        print("llama7b_c2_p512.npz written")
+        return
     np.savez_compressed(os.path.join(HERE, "ref_kernels.npz"), **ref_kernels(ref))
     print("ref_kernels.npz written")
     np.savez_compressed(os.path.join(HERE, "tiny_c0.npz"), **tiny_c0(ref))
@@ -211,6 +266,8 @@ def main():
     if not a.skip_7b:
         np.savez_compressed(os.path.join(HERE, "llama7b_c2.npz"), **llama7b(ref))
         print("llama7b_c2.npz written")
+        np.savez_compressed(os.path.join(HERE, "llama7b_c2_p512.npz"), **llama7b_long(ref))
+        print("llama7b_c2_p512.npz written")
 
 
 if __name__ == "__main__":

@@ -93,3 +93,69 @@ def test_7b_layer_activations(cuda, golden, engine7b, kv):
         assert elementwise_ok(lg, ref_logits).all()
     np.testing.assert_allclose(np.linalg.norm(taps, axis=1), golden[f"{kv}_tap_norms_last_prompt"], rtol=TOL)
     kvc.close()
+
+
+# ---------------------------------------------------------------- the benchmarked configuration
+# A 512-token prompt, then greedy decode at contexts 513-544, as bench.py runs it (fp16 KV),
+# and with the fp32 cache the reference engine itself uses.
+
+@pytest.fixture(scope="module")
+def golden512():
+    path = os.path.join(GOLDEN, "llama7b_c2_p512.npz")
+    if not os.path.exists(path):
+        pytest.skip("llama7b_c2_p512.npz not generated")
+    return np.load(path)
+
+
+def _check_taps(taps, logits, g, kv, tag):
+    layers = [int(l) for l in g["tap_layers"]]
+    ref_logits = g[f"{kv}_logits_{tag}"]
+    assert rel_l2(logits, ref_logits) <= TOL, f"{tag}: logits relative error {rel_l2(logits, ref_logits)}"
+    assert int(np.argmax(logits)) == int(np.argmax(ref_logits))
+    for i, l in enumerate(layers):
+        ref = g[f"{kv}_taps_{tag}"][i]
+        assert rel_l2(taps[l], ref) <= TOL, f"{tag} layer {l}: relative error {rel_l2(taps[l], ref)}"
+        if kv == "kv32":
+            ok = elementwise_ok(taps[l], ref)
+            assert ok.all(), f"{tag} layer {l}: {(~ok).sum()} elements outside the elementwise 1e-2 form"
+    np.testing.assert_allclose(np.linalg.norm(taps, axis=1), g[f"{kv}_tap_norms_{tag}"], rtol=TOL)
+
+
+@pytest.mark.parametrize("kv", ["kv16", "kv32"])
+def test_7b_prompt512_tokens_and_taps(cuda, golden512, engine7b, kv):
+    """Positions 0-510 as one device decode, position 511 (last prompt token) through
+    forward_single_token with taps, 512-542 as a second device decode continuing the
+    same cache, and 543 through forward_single_token with taps: the 32 generated
+    tokens and the final argmax must equal the oracle's, the taps and logits at 511
+    and 543 be within 1e-2."""
+    eng, g = engine7b, golden512
+    prompt = g["prompt"]
+    want = g[f"{kv}_tokens"]
+    n_prompt = len(prompt)
+    n_gen = len(want) - 1 - n_prompt
+    assert n_prompt == 512 and n_gen == 32
+    kvc = cuda.KVCache(eng, n_prompt + n_gen + 1, cuda.BT_KV_FP32 if kv == "kv32" else cuda.BT_KV_FP16)
+    got = list(eng.decode(kvc, prompt[:n_prompt - 1], n_gen=0)[:n_prompt - 1])
+    eng.set_taps(True)
+    try:
+        lg = eng.forward_single_token(int(prompt[n_prompt - 1]), n_prompt - 1, kvc)
+        _check_taps(eng.read_taps(), lg, g, kv, "last_prompt")
+        got.append(int(prompt[n_prompt - 1]))
+        first = eng.last_argmax
+        eng.set_taps(False)
+        mid = eng.decode(kvc, [first], n_gen=n_gen - 2, pos0=n_prompt)  # positions 512 .. 542
+        got.extend(int(t) for t in mid[:-1])
+        last = int(mid[-1])
+        eng.set_taps(True)
+        lg = eng.forward_single_token(last, n_prompt + n_gen - 1, kvc)
+        _check_taps(eng.read_taps(), lg, g, kv, "last_gen")
+        got.append(last)
+        got.append(eng.last_argmax)
+    finally:
+        eng.set_taps(False)
+    got = np.array(got, np.uint32)
+    assert len(got) == len(want)
+    assert np.array_equal(got[:n_prompt], prompt)
+    bad = np.nonzero(got != want)[0]
+    assert bad.size == 0, f"greedy tokens differ at positions {bad[:8]} (margins {g[f'{kv}_margins'][bad[:8] - 1]})"
+    kvc.close()

@@ -158,6 +158,53 @@ def test_gemv_units_vs_oracle(cuda, oracle, torch_mod, M, K):
     assert (err <= 1e-5 * mag + 1e-30).all(), f"worst relative error {np.max(err / (mag + 1e-30))}"
 
 
+def outlier_case(oracle, M, K, seed):
+    """x N(0,1) with one block scaled by 1e4 and another by 1e3; the weights of those two
+    blocks are zero in the even rows, so the even rows' true sums are made of the
+    ordinary blocks only and an error proportional to the outliers would show there."""
+    rng = np.random.default_rng(seed)
+    b = oracle.quantize_q8_0((rng.standard_normal(M * K) * 0.02).astype(np.float32))
+    x = rng.standard_normal(K).astype(np.float32)
+    nb = K // 32
+    big, mid = nb // 3, (2 * nb) // 3
+    x[32 * big:32 * big + 32] *= 1e4
+    x[32 * mid:32 * mid + 32] *= 1e3
+    qs = b["qs"].reshape(M, nb, 32)
+    qs[0::2, big] = 0
+    qs[0::2, mid] = 0
+    want = oracle.matvec_q8_0(b, x, M, K, nthreads=8)
+    mag = np.abs(b["scale"].reshape(M, nb, 1) * qs.astype(np.float64) * np.abs(x.reshape(1, nb, 32))).sum(axis=(1, 2))
+    return b, x, want, mag
+
+
+@pytest.mark.parametrize("M,K", [(4096, 4096), (1000, 11008)])
+def test_gemv_units_outlier_blocks(cuda, oracle, torch_mod, M, K):
+    """Outlier activations: every block keeps 22 bits relative to its own max, so rows that
+    do not touch the outlier blocks stay within the GEMV bar of their own magnitude."""
+    b, x, want, mag = outlier_case(oracle, M, K, seed=M + K)
+    units = cuda.pack_q8_units(dev(torch_mod, b.view(np.uint8)), M, K)
+    got = cuda.gemv_q8_units(units, dev(torch_mod, x), M, K).cpu().numpy()
+    err = np.abs(got.astype(np.float64) - want)
+    assert (err <= 1e-5 * mag + 1e-30).all(), f"worst relative error {np.max(err / (mag + 1e-30))}"
+
+
+def test_gemv_units_timeout_is_reported(cuda, torch_mod):
+    """A device wait that gave up (injected on the host) turns into BT_ERR_DEVICE_TIMEOUT
+    on the next call, and the call after it is valid again."""
+    from blocktensor_b200 import native
+    M, K = 256, 256
+    rng = np.random.default_rng(1)
+    w = dev(torch_mod, (rng.standard_normal(M * K) * 0.02).astype(np.float32))
+    units = cuda.pack_q8_units(cuda.quantize_q8_0(w), M, K)
+    x = dev(torch_mod, rng.standard_normal(K).astype(np.float32))
+    good = cuda.gemv_q8_units(units, x, M, K).cpu().numpy()
+    native.call("bt_cuda_gemv_inject_timeout", torch_mod.cuda.current_device(), 0)
+    with pytest.raises(native.CudaBackendError) as ei:
+        cuda.gemv_q8_units(units, x, M, K)
+    assert ei.value.code == native.BT_ERR_DEVICE_TIMEOUT
+    assert np.array_equal(cuda.gemv_q8_units(units, x, M, K).cpu().numpy(), good)
+
+
 def test_gemv_units_deterministic_and_repeatable(cuda, oracle, torch_mod):
     M, K = 4096, 4096
     rng = np.random.default_rng(5)
