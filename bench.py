@@ -152,6 +152,82 @@ def trace_summary(tr: np.ndarray, n_layers: int) -> dict:
     return res
 
 
+# ---------------------------------------------------------------- diagnostics: GEMV microbenchmark, tiny model
+
+def c1_gemv(torch, bt, dev, log):
+    """The dequant-GEMV microbenchmark: W 4096 x 4096 int8 (uniform [-127, 127]) with fp32
+    scales per 32-block (U(0.001, 0.02)), x [B, 4096] fp32 N(0, 1), y = x W^T, B in {1, 4, 16}.
+    16 copies of W (302 MB, over twice L2) are cycled so every launch streams W from HBM.
+    HBM bytes per launch: W (int8 + scales) + x + y."""
+    import ctypes
+    M = K = 4096
+    copies = 16
+    peak, _ = hbm_peak()
+    g = torch.Generator(device=f"cuda:{dev}").manual_seed(0)
+    qs = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=f"cuda:{dev}", generator=g)
+    sc = torch.rand((M, K // 32), device=f"cuda:{dev}", generator=g) * 0.019 + 0.001
+    blocks = torch.empty((M * K // 32, 36), dtype=torch.uint8, device=f"cuda:{dev}")
+    blocks[:, :4] = sc.reshape(-1, 1).view(torch.uint8).reshape(-1, 4)
+    blocks[:, 4:] = qs.reshape(-1, 32).view(torch.uint8)
+    units = bt.pack_q8_units(blocks, M, K)
+    ub = units.numel()
+    units_all = units.repeat(copies)
+    split = torch.cat([qs.view(torch.uint8).reshape(-1), sc.reshape(-1).view(torch.uint8)])
+    sb = split.numel()
+    split_all = split.repeat(copies)
+    out = []
+    lib = bt.load()
+    for B in (1, 4, 16):
+        x = torch.randn((B, K), device=f"cuda:{dev}", generator=g)
+        y = torch.empty((B, M), device=f"cuda:{dev}")
+        w_bytes = M * K + M * (K // 32) * 4
+        nbytes = w_bytes + 4 * B * K + 4 * B * M
+        for kind, name, w, stride in ((0, "tcgen05 GEMV (tile layout)", units_all, ub),
+                                      (1, "tcgen05 GEMM (tile layout, token image)", units_all, ub),
+                                      (2, "CUDA-core GEMV (split layout)", split_all, sb)):
+            if kind == 0 and B != 1:
+                continue
+            us = ctypes.c_float()
+            bt.native.check(lib.bt_cuda_gemv_bench(kind, w.data_ptr(), x.data_ptr(), y.data_ptr(), M, K, B, copies,
+                                                   stride, 200, None, ctypes.byref(us)))
+            gbs = nbytes / (us.value * 1e-6) / 1e9
+            out.append({"B": B, "kernel": name, "us": round(us.value, 2), "GBps": round(gbs, 1),
+                        "frac_of_measured_hbm": round(gbs / peak, 3), "bytes": nbytes})
+    log("[ours] C1 GEMV: " + json.dumps(out))
+    return out
+
+
+def c0_tiny(torch, bt, dev, log):
+    """The tiny Llama-style config (D288 F768 L6 H6 V32000): 16-token prompt (prefilled), then
+    128 greedy decode steps at batch 1 with an fp32 KV cache, device-timed."""
+    from blocktensor_b200 import synthetic
+    cfg = synthetic.config("tiny", 256)
+    eng = bt.TransformerEngine(cfg, device=dev)
+    eng.generate(seed=0, sigma=0.02)
+    kv = bt.KVCache(eng, 256, bt.BT_KV_FP32)
+    prompt = synthetic.tokens(0, 16, cfg.vocab_size)
+    eng.prefill(kv, prompt)
+    eng.steps(kv, 1)
+    torch.cuda.synchronize()
+    stream = torch.cuda.ExternalStream(eng.stream_handle, device=torch.device("cuda", dev))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 128
+    e0.record(stream)
+    eng.steps(kv, n, stream=eng.stream_handle)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    nbytes = sum(synthetic.step_bytes(cfg, 17 + i + 1, 4) for i in range(n)) / n
+    peak, _ = hbm_peak()
+    gbs = nbytes / (ms / n * 1e-3) / 1e9
+    kv.close()
+    eng.close()
+    res = {"tokens_per_s": round(n / (ms / 1000.0), 1), "us_per_token": round(ms / n * 1000.0, 1),
+           "bytes_per_token": int(nbytes), "GBps": round(gbs, 1), "frac_of_measured_hbm": round(gbs / peak, 4)}
+    log("[ours] C0 tiny decode: " + json.dumps(res))
+    return res
+
+
 # ---------------------------------------------------------------- CPU reference
 
 def cpu_reference_tokens_per_s(n_tokens: int, warmup: int, budget_s: float, log=print):
@@ -252,11 +328,25 @@ def run_ours(args):
     log(f"[ours] {shape}: weights generated on device in {time.time() - t0:.1f} s")
     prompt = synthetic.tokens(rank if tpw == 1 else 0, prompt_len, cfg.vocab_size)
     t0 = time.time()
-    eng.begin(kv, prompt)
-    eng.steps(kv, prompt_len)          # prompt, one position per step (untimed)
+    prompt_info = None
+    if tpw == 1 and not args.no_prefill:
+        # the prompt's positions but the last as batched tensor-core GEMMs (bt_engine_prefill),
+        # timed on the host around the call (it returns when done); the last prompt token is
+        # the first decode step
+        torch.cuda.synchronize()
+        tp0 = time.perf_counter()
+        eng.prefill(kv, prompt)
+        pf_s = time.perf_counter() - tp0
+        prompt_info = {"api": "bt_engine_prefill", "positions": prompt_len - 1, "seconds": pf_s,
+                       "tokens_per_s": (prompt_len - 1) / pf_s}
+        eng.steps(kv, 1)
+    else:
+        eng.begin(kv, prompt)
+        eng.steps(kv, prompt_len)      # prompt, one position per step (untimed)
     eng.steps(kv, W)                   # warm-up decode steps
     torch.cuda.synchronize()
-    log(f"[ours] prompt {prompt_len} + warm-up {W} steps in {time.time() - t0:.1f} s")
+    log(f"[ours] prompt {prompt_len} + warm-up {W} steps in {time.time() - t0:.1f} s"
+        + (f" (prefill {prompt_info['tokens_per_s']:.0f} tokens/s)" if prompt_info else ""))
 
     stream = torch.cuda.ExternalStream(eng.stream_handle, device=torch.device("cuda", local))
     ev0 = torch.cuda.Event(enable_timing=True)
@@ -339,6 +429,11 @@ def run_ours(args):
         eng.set_trace(False)
         log("[ours] phase timeline (us): " + json.dumps(timeline))
 
+    diag = None
+    if rank == 0 and world == 1 and not args.no_diagnostics and not args.layers:
+        diag = {"prompt_prefill": prompt_info, "c1_gemv": c1_gemv(torch, bt, local, log),
+                "c0_tiny_decode": c0_tiny(torch, bt, local, log)}
+
     # DRAM bytes per launch of the step kernel from an ncu capture (profiles/), scaled to this model
     traffic = None
     tfile = os.path.join(ROOT, "profiles", "decode_step_traffic.json")
@@ -382,6 +477,7 @@ def run_ours(args):
                     "d2h_bytes_per_step": vocab_local * 4 + 32,
                     "api": "bt_engine_forward_token(host token, host logits)"},
             "gpu_launches": launches,
+            "diagnostics": diag,
             "clocks": clk,
             "cpu_baseline": cpu,
         }
@@ -405,6 +501,10 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="also time the launch-per-operation step (per-kernel breakdown, diagnostic)")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="run the prompt one decode step per position instead of bt_engine_prefill")
+    ap.add_argument("--no-diagnostics", action="store_true",
+                    help="skip the GEMV microbenchmark and tiny-model lines of the diagnostics")
     ap.add_argument("--trace", action="store_true",
                     help="also record one step's per-phase device timestamps (diagnostic, untimed)")
     ap.add_argument("--replicas", action="store_true",

@@ -348,6 +348,8 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_digits_kernel(UnitW W, Gemm
         for (uint32_t st = 0; st < nst; ++st) {
             const uint32_t b0 = st * kGStageBlocks, n = min(kGStageBlocks, NB - b0);
             const uint8_t* stage = ring + (size_t)s * kGStageBytes;
+            // the scales and block factors this warp reads were written by the stage's bulk copies
+            if (ok) ok = mbar_wait(&full[s], ph, err);
             for (uint32_t k = 0; k < n; ++k, ++j) {
                 const uint32_t slot = j % kGSlots, use = j / kGSlots;
                 if (ok) ok = mbar_wait(&tfull[slot], use & 1, err);

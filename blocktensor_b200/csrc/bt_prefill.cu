@@ -205,6 +205,17 @@ int prefill_chunk_t(bt_engine* e, bt_kv* kv, uint32_t T, uint32_t pos0, cudaStre
 }
 
 }  // namespace
+
+cudaError_t gemm_units_launch(const void* units, const float* X, float* Y, uint32_t M, uint32_t K, uint32_t T,
+                              uint8_t* img, uint32_t* err, uint32_t nsm, cudaStream_t s) {
+    cudaError_t ce = launch_token_image(X, nullptr, nullptr, T, K, img, nullptr, nullptr, s);
+    if (ce != cudaSuccess) return ce;
+    return launch_gemm_digits(UnitW{static_cast<const uint8_t*>(units), M, unit_rows(M), K}, GemmIn{img, nullptr, 0.0f, T},
+                              GEpiStore{Y, M}, err, nsm, s);
+}
+
+size_t gemm_units_scratch(uint32_t K, uint32_t T) { return token_image_bytes(T, K); }
+
 }  // namespace bt
 
 extern "C" {
@@ -280,10 +291,7 @@ int bt_cuda_gemm_q8_units(const void* units, const float* X, float* Y, uint32_t 
     BT_CUDA_CHECK(cudaMallocAsync(reinterpret_cast<void**>(&ws), img_bytes + 256, s));
     uint32_t* err = reinterpret_cast<uint32_t*>(ws + img_bytes);
     cudaError_t ce = cudaMemsetAsync(err, 0, sizeof(uint32_t), s);
-    if (ce == cudaSuccess) ce = launch_token_image(X, nullptr, nullptr, T, K, ws, nullptr, nullptr, s);
-    if (ce == cudaSuccess)
-        ce = launch_gemm_digits(UnitW{static_cast<const uint8_t*>(units), M, unit_rows(M), K},
-                                GemmIn{ws, nullptr, 0.0f, T}, GEpiStore{Y, M}, err, (uint32_t)nsm, s);
+    if (ce == cudaSuccess) ce = gemm_units_launch(units, X, Y, M, K, T, ws, err, (uint32_t)nsm, s);
     uint32_t flag = 0;
     if (ce == cudaSuccess) ce = cudaMemcpyAsync(&flag, err, sizeof(flag), cudaMemcpyDeviceToHost, s);
     const cudaError_t ce2 = cudaFreeAsync(ws, s);

@@ -397,6 +397,56 @@ int bt_cuda_gemv_q8_units(const void* units, const float* x, float* y, uint32_t 
     return gemv_check_timeout(ws->ticket + kWsTickets, ws->ticket, sizeof(uint32_t) * kWsTickets, s);
 }
 
+int bt_cuda_gemv_bench(int kind, const void* w, const float* X, float* Y, uint32_t M, uint32_t K, uint32_t B,
+                       uint32_t n_copies, uint64_t copy_stride, uint32_t iters, void* stream, float* us_per_call) {
+    BT_CHECK_ARG(w && X && Y && us_per_call, "gemv_bench: null argument");
+    BT_CHECK_ARG(K % 32 == 0 && K > 0 && K <= kGemvMaxK && M > 0, "gemv_bench: bad shape");
+    BT_CHECK_ARG(n_copies >= 1 && iters >= 1 && B >= 1, "gemv_bench: bad count");
+    BT_CHECK_ARG(kind != 0 || B == 1, "gemv_bench: the tile-layout GEMV takes one vector");
+    BT_CHECK_ARG(kind != 2 || B <= 16, "gemv_bench: the split-layout GEMV takes at most 16 vectors");
+    BT_CHECK_ARG(kind >= 0 && kind <= 2, "gemv_bench: kind must be 0, 1 or 2");
+    BT_CHECK_ARG(M <= kWsTickets * kTileRows, "gemv_bench: M too large");
+    cudaStream_t s = as_stream(stream);
+    int dev = 0;
+    BT_CUDA_CHECK(cudaGetDevice(&dev));
+    GemvWorkspace* ws = nullptr;
+    int rc = gemv_workspace(dev, &ws);
+    if (rc != BT_OK) return rc;
+    uint8_t* img = nullptr;
+    if (kind == 1) BT_CUDA_CHECK(cudaMallocAsync(reinterpret_cast<void**>(&img), gemm_units_scratch(K, B), s));
+    cudaEvent_t e0, e1;
+    BT_CUDA_CHECK(cudaEventCreate(&e0));
+    BT_CUDA_CHECK(cudaEventCreate(&e1));
+    auto one = [&](uint32_t i) -> cudaError_t {
+        const uint8_t* wi = static_cast<const uint8_t*>(w) + (uint64_t)(i % n_copies) * copy_stride;
+        if (kind == 0)
+            return launch_gemv_mma(UnitW{wi, M, unit_rows(M), K}, MProCopy{X}, SEpiStore{Y},
+                                   SplitScratch{ws->part, ws->ticket}, ws->ticket + kWsTickets, ws->nsm, s, false);
+        if (kind == 1) return gemm_units_launch(wi, X, Y, M, K, B, img, ws->ticket + kWsTickets, ws->nsm, s);
+        const int8_t* qs = reinterpret_cast<const int8_t*>(wi);
+        const float* sc = reinterpret_cast<const float*>(wi + (uint64_t)M * K);
+        if (B == 1) return launch_gemv(GemvW{qs, sc, M, K}, ProCopy{X}, EpiStore{Y}, s, false);
+        if (B == 2) return launch_gemv_batch<2>(qs, sc, X, Y, M, K, B, s);
+        if (B <= 4) return launch_gemv_batch<4>(qs, sc, X, Y, M, K, B, s);
+        if (B <= 8) return launch_gemv_batch<8>(qs, sc, X, Y, M, K, B, s);
+        return launch_gemv_batch<16>(qs, sc, X, Y, M, K, B, s);
+    };
+    cudaError_t ce = cudaSuccess;
+    for (uint32_t i = 0; i < 3 && ce == cudaSuccess; ++i) ce = one(i);  // warm-up
+    if (ce == cudaSuccess) ce = cudaEventRecord(e0, s);
+    for (uint32_t i = 0; i < iters && ce == cudaSuccess; ++i) ce = one(i);
+    if (ce == cudaSuccess) ce = cudaEventRecord(e1, s);
+    if (ce == cudaSuccess) ce = cudaEventSynchronize(e1);
+    float ms = 0.0f;
+    if (ce == cudaSuccess) ce = cudaEventElapsedTime(&ms, e0, e1);
+    if (img) cudaFreeAsync(img, s);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (ce != cudaSuccess) return fail(BT_ERR_CUDA, std::string("gemv_bench: ") + cudaGetErrorString(ce));
+    *us_per_call = ms * 1000.0f / (float)iters;
+    return gemv_check_timeout(ws->ticket + kWsTickets, ws->ticket, sizeof(uint32_t) * kWsTickets, s);
+}
+
 int bt_cuda_gemv_inject_timeout(int device, int noalloc) {
     int prev = 0;
     BT_CUDA_CHECK(cudaGetDevice(&prev));

@@ -89,6 +89,7 @@ SIGNATURES = {
     "bt_cuda_gemv_q8_units": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp]),
     "bt_cuda_gemv_q8_units_noalloc": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp]),
     "bt_cuda_gemv_inject_timeout": (_i32, [_i32, _i32]),
+    "bt_cuda_gemv_bench": (_i32, [_i32, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u64, _u32, _vp, C.POINTER(_f32)]),
     "bt_cuda_rmsnorm": (_i32, [_vp, _vp, _vp, _u32, _u32, _f32, _vp]),
     "bt_cuda_rope": (_i32, [_vp, _vp, _u32, _u32, _u32, _u32, _f32, _vp]),
     "bt_cuda_softmax": (_i32, [_vp, _vp, _u32, _u32, _vp]),

@@ -187,6 +187,19 @@ BT_API int bt_cuda_gemv_q8_units(const void* units, const float* x, float* y, ui
 BT_API int bt_cuda_gemv_q8_units_noalloc(const void* units, const float* x, float* y, uint32_t M, uint32_t K,
                                          void* stream);
 
+/* Microbenchmark of the standalone int8 GEMV/GEMM kernels (no counterpart in
+ * the reference; the dequant-GEMV benchmark): `iters` launches of kernel
+ * `kind` back to back on `stream` after 3 warm-up launches, cycling through
+ * n_copies weight copies copy_stride bytes apart (together larger than L2,
+ * every launch streams its weights from HBM), reporting the mean device time
+ * per launch from CUDA events.  kind 0: tensor-core GEMV on the tile layout
+ * (B = 1); kind 1: tensor-core GEMM on the tile layout for B token rows (its
+ * token image included); kind 2: CUDA-core GEMV on the split layout, qs
+ * [M][K] followed by the scales [M][K/32] (B <= 16).  X [B][K], Y [B][M]. */
+BT_API int bt_cuda_gemv_bench(int kind, const void* w, const float* X, float* Y, uint32_t M, uint32_t K, uint32_t B,
+                              uint32_t n_copies, uint64_t copy_stride, uint32_t iters, void* stream,
+                              float* us_per_call);
+
 /* Fault injection on the host, for tests of the standalone GEMVs' timeout
  * reporting (no counterpart in the reference): sets the bounded-wait flag of
  * bt_cuda_gemv_q8_units (noalloc = 0) or of bt_cuda_gemv_q8_units_noalloc

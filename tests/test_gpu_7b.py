@@ -159,3 +159,32 @@ def test_7b_prompt512_tokens_and_taps(cuda, golden512, engine7b, kv):
     bad = np.nonzero(got != want)[0]
     assert bad.size == 0, f"greedy tokens differ at positions {bad[:8]} (margins {g[f'{kv}_margins'][bad[:8] - 1]})"
     kvc.close()
+
+
+@pytest.mark.parametrize("kv", ["kv16", "kv32"])
+def test_7b_prompt512_prefill(cuda, golden512, engine7b, kv):
+    """The 512-token prompt through prefill (positions 0-510 as batched GEMMs), the last
+    prompt position through the decode step with taps, then 32 greedy steps: taps and
+    logits at position 511 within 1e-2 and the 32 generated tokens identical."""
+    eng, g = engine7b, golden512
+    prompt = g["prompt"]
+    want = g[f"{kv}_tokens"]
+    n_prompt, n_gen = 512, 32
+    kvc = cuda.KVCache(eng, n_prompt + n_gen + 1, cuda.BT_KV_FP32 if kv == "kv32" else cuda.BT_KV_FP16)
+    eng.prefill(kvc, prompt)
+    eng.set_taps(True)
+    try:
+        eng.steps(kvc, 1)
+        taps = eng.read_taps()
+    finally:
+        eng.set_taps(False)
+    layers = [int(l) for l in g["tap_layers"]]
+    for i, l in enumerate(layers):
+        ref = g[f"{kv}_taps_last_prompt"][i]
+        assert rel_l2(taps[l], ref) <= TOL, f"layer {l}: relative error {rel_l2(taps[l], ref)}"
+    np.testing.assert_allclose(np.linalg.norm(taps, axis=1), g[f"{kv}_tap_norms_last_prompt"], rtol=TOL)
+    eng.steps(kvc, n_gen)  # positions 512 .. 543
+    got = kvc.read_tokens(0, n_prompt + n_gen + 1)
+    bad = np.nonzero(got != want)[0]
+    assert bad.size == 0, f"greedy tokens differ at positions {bad[:8]} (margins {g[f'{kv}_margins'][bad[:8] - 1]})"
+    kvc.close()
