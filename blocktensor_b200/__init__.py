@@ -228,6 +228,17 @@ class TransformerEngine:
     def __exit__(self, *exc):
         self.close()
 
+    @classmethod
+    def from_btmodel(cls, path: str, device: int = 0) -> "TransformerEngine":
+        """An engine loaded from a .btmodel file of either version (v2 carries the RoPE base;
+        v1, the reference's format, uses cpu_ref::rope's 10000)."""
+        from . import btmodel
+        m = btmodel.read_btmodel_any(path)
+        eng = cls(m.config, device=device, rope_theta=getattr(m, "rope_theta", 10000.0))
+        eng.load(m.tensors)
+        eng.kv_dtype_hint = BT_KV_FP16 if getattr(m, "kv_dtype", 0) == 1 else BT_KV_FP32
+        return eng
+
     def load(self, tensors: Sequence, on_device: bool = False):
         """tensors: buffers (numpy arrays, or CUDA tensors with on_device=True) in .btmodel order."""
         n = len(tensors)
@@ -341,6 +352,51 @@ class TransformerEngine:
     @property
     def stream_handle(self) -> int:
         return load().bt_engine_stream(self._h) or 0
+
+
+class Batch:
+    """Independent sequences decoded together (bt_batch_*): one token row per sequence in
+    every tensor-core GEMM, attention per sequence over its own cache."""
+
+    def __init__(self, engine: TransformerEngine, n_seq: int, max_seq: int, kv_dtype: int = BT_KV_FP32):
+        self.engine = engine
+        self.n_seq, self.max_seq = n_seq, max_seq
+        h = C.c_void_p()
+        call("bt_batch_create", engine.handle, n_seq, max_seq, kv_dtype, C.byref(h))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            load().bt_batch_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def prefill(self, s: int, prompt: Sequence[int]):
+        p = np.ascontiguousarray(np.asarray(prompt, dtype=np.uint32))
+        call("bt_batch_prefill", self._h, s, p.ctypes.data, len(p))
+
+    def steps(self, n: int, stream=None):
+        call("bt_batch_steps", self._h, n, stream)
+
+    def read_tokens(self, s: int, pos0: int, n: int) -> np.ndarray:
+        out = np.zeros(n, np.uint32)
+        call("bt_batch_read_tokens", self._h, s, pos0, n, out.ctypes.data)
+        return out
+
+    def read_logits(self) -> np.ndarray:
+        out = np.zeros((self.n_seq, self.engine.config.vocab_size), np.float32)
+        call("bt_batch_read_logits", self._h, out.ctypes.data)
+        return out
+
+    def step_bytes(self) -> int:
+        b = C.c_uint64()
+        call("bt_batch_step_info", self._h, C.byref(b))
+        return b.value
 
 
 class KVCache:

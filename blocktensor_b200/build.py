@@ -16,7 +16,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libbt_cuda.so")
 
-SOURCES = ["bt_quant.cu", "bt_prims.cu", "bt_engine.cu", "bt_noalloc.cu", "bt_prefill.cu"]
+SOURCES = ["bt_quant.cu", "bt_prims.cu", "bt_engine.cu", "bt_noalloc.cu", "bt_prefill.cu", "bt_batch.cu", "bt_q4.cu", "bt_sample.cu"]
 HEADERS = ["bt_common.cuh", "bt_gemv.cuh", "bt_gemv_mma.cuh", "bt_ptx.cuh", "bt_attention.cuh", "bt_step.cuh",
            "bt_gemm.cuh", "bt_engine_impl.h", "bt_internal.h"]
 

@@ -106,6 +106,12 @@ void CudaBackend::dispatch(const std::shared_ptr<IComputePipeline>& pipeline,
         bt_throw_if_error(bt_cuda_matvec_q8_0(dptr(buffers[0], "W"), static_cast<const float*>(dptr(buffers[1], "X")),
                                               static_cast<float*>(dptr(buffers[2], "Y")), u[0], u[1], nullptr),
                           "matvec_q8_0");
+    } else if (n == "matvec_q4_0") {
+        need(3, 8);
+        std::memcpy(u, push, 8);
+        bt_throw_if_error(bt_cuda_matvec_q4_0(dptr(buffers[0], "W"), static_cast<const float*>(dptr(buffers[1], "X")),
+                                              static_cast<float*>(dptr(buffers[2], "Y")), u[0], u[1], nullptr),
+                          "matvec_q4_0");
     } else if (n == "rmsnorm") {
         need(3, 8);
         float eps;

@@ -12,8 +12,8 @@ CudaTransformerEngine::CudaTransformerEngine(std::shared_ptr<IComputeBackend> ba
                                              const TransformerWeights& weights, float rope_theta, int kv_dtype)
     : backend_(std::move(backend)), cfg_(weights.config), kv_dtype_(kv_dtype) {
     if (!backend_) throw std::invalid_argument("CudaTransformerEngine: null backend");
-    if (weights.quant_type != DataType::INT8)
-        throw std::invalid_argument("CudaTransformerEngine: only INT8 (Q8_0) weights are supported");
+    if (weights.quant_type != DataType::INT8 && weights.quant_type != DataType::INT4)
+        throw std::invalid_argument("CudaTransformerEngine: weights must be INT8 (Q8_0) or INT4 (Q4_0)");
     if (auto cb = std::dynamic_pointer_cast<CudaBackend>(backend_)) device_ = cb->device();
     bt_model_config c;
     static_assert(sizeof(c) == sizeof(cfg_), "config size");

@@ -611,7 +611,11 @@ int bt_engine_load(bt_engine* e, const bt_tensor_view* t, uint32_t n, int on_dev
         return fail(BT_ERR_INVALID_ARGUMENT, "bt_engine_load: expected 3 + 9*num_layers tensors");
     DeviceGuard guard(e->device);
     const size_t D = c.dim, F = c.hidden_dim, KV = kvd(c), V = c.vocab_size;
-    auto qbytes = [](size_t r, size_t k) { return r * k / 32 * 36; };
+    // Q8_0 (36-byte blocks) or Q4_0 (20-byte blocks, quant_types.hpp:17-20) matrices, told apart
+    // by the head matrix's size; every matrix of a model has the same type (one quant_type per
+    // .btmodel, model_importer.cpp:55-57)
+    const size_t blk_bytes = (n > 2 && t[2].bytes == V * D / 32 * 20) ? 20 : 36;
+    auto qbytes = [blk_bytes](size_t r, size_t k) { return r * k / 32 * blk_bytes; };
     // size checks (the reference reads raw sizes; a mismatch is a corrupt model)
     auto expect = [&](uint32_t i, size_t bytes, const char* what) -> int {
         if (t[i].bytes != bytes || (!t[i].data && bytes))
@@ -641,13 +645,16 @@ int bt_engine_load(bt_engine* e, const bt_tensor_view* t, uint32_t n, int on_dev
     if (!on_device) BT_CUDA_CHECK(cudaMalloc(&stage, max_q));
     // this rank's rows (and, for o and down, its columns) of a tensor
     auto load_q = [&](const bt_tensor_view& tv, const Slot& sl) -> int {
-        const size_t row_bytes = (size_t)sl.gcols / 32 * 36;
+        const size_t row_bytes = (size_t)sl.gcols / 32 * blk_bytes;
         const void* src = static_cast<const uint8_t*>(tv.data) + (size_t)sl.grow0 * row_bytes;
         if (!on_device) {
             BT_CUDA_CHECK(cudaMemcpyAsync(stage, src, (size_t)sl.rows * row_bytes, cudaMemcpyHostToDevice, s));
             src = stage;
         }
-        BT_CUDA_CHECK(launch_pack_units(src, sl.units, sl.rows, sl.cols, sl.map, s, sl.gcols / 32, sl.cb0));
+        if (blk_bytes == 20)
+            BT_CUDA_CHECK(launch_pack_units_q4(src, sl.units, sl.rows, sl.cols, sl.map, s, sl.gcols / 32, sl.cb0));
+        else
+            BT_CUDA_CHECK(launch_pack_units(src, sl.units, sl.rows, sl.cols, sl.map, s, sl.gcols / 32, sl.cb0));
         if (!on_device) BT_CUDA_CHECK(cudaStreamSynchronize(s));  // stage is reused
         return BT_OK;
     };
@@ -935,7 +942,10 @@ int bt_engine_set_trace(bt_engine* e, int enable) {
     DeviceGuard guard(e->device);
     BT_CUDA_CHECK(cudaStreamSynchronize(e->stream));
     if (enable && !e->trace) {
-        const size_t n = (size_t)(5 * e->lc.num_layers + 1) * e->num_sms * kTraceSlots;
+        size_t n = (size_t)(5 * e->lc.num_layers + 1) * e->num_sms * kTraceSlots;
+#ifdef BT_STAGE_TRACE
+        n += (size_t)e->num_sms * kStageTraceMax * 4;
+#endif
         BT_TRY_ALLOC(e->allocs, &e->trace, n, "step trace");
         BT_CUDA_CHECK(cudaMemset(e->trace, 0, n * sizeof(uint64_t)));
     }
@@ -954,8 +964,11 @@ int bt_engine_set_trace(bt_engine* e, int enable) {
 int bt_engine_read_trace(bt_engine* e, uint64_t* out, uint64_t n_words) {
     if (!e || !out) return fail(BT_ERR_INVALID_ARGUMENT, "null argument");
     if (!e->trace) return fail(BT_ERR_INVALID_ARGUMENT, "trace is off (bt_engine_set_trace)");
-    const uint64_t n = (uint64_t)(5 * e->lc.num_layers + 1) * e->num_sms * kTraceSlots;
-    if (n_words != n) return fail(BT_ERR_INVALID_ARGUMENT, "read_trace: n_words must be (5 L + 1) * SMs * 8");
+    uint64_t n = (uint64_t)(5 * e->lc.num_layers + 1) * e->num_sms * kTraceSlots;
+#ifdef BT_STAGE_TRACE
+    n += (uint64_t)e->num_sms * kStageTraceMax * 4;  // a stage-trace build: the stage timeline follows
+#endif
+    if (n_words != n) return fail(BT_ERR_INVALID_ARGUMENT, "read_trace: n_words does not match the trace size");
     DeviceGuard guard(e->device);
     BT_CUDA_CHECK(cudaStreamSynchronize(e->stream));
     BT_CUDA_CHECK(cudaMemcpy(out, e->trace, n * sizeof(uint64_t), cudaMemcpyDeviceToHost));

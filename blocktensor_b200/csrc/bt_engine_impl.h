@@ -114,6 +114,23 @@ struct bt_kv {
 
 namespace bt {
 
+// One sequence's KV cache as prefill sees it: K and V [L][KVH][max_seq][hd] (fp32 or
+// fp16 by the engine call), the RoPE table, and the flag bounded waits set.
+struct CacheRef {
+    void* k;
+    void* v;
+    const float2* rope;
+    uint32_t max_seq;
+    uint32_t* err;
+};
+
+// Prompt prefill building blocks (bt_prefill.cu).
+int ensure_prefill_buffers(bt_engine* e);
+template <typename KVT>
+int prefill_chunk_t(bt_engine* e, const CacheRef& kv, uint32_t T, uint32_t pos0, cudaStream_t s);
+cudaError_t launch_token_image(const float* src, const uint32_t* tokens, const float* w, uint32_t T, uint32_t K,
+                               uint8_t* img, float* ss, float* x_out, cudaStream_t s);
+
 struct DeviceGuard {
     int prev = -1;
     explicit DeviceGuard(int dev) {

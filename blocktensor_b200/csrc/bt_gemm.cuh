@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_digits_kernel(UnitW W, Gemm
 // embedding rows of `tokens`) times the RMSNorm weight w (null: none), plus the
 // per-block sums of squares of the unweighted rows; x_out (non-null) receives
 // the rows themselves (the residual stream of layer 0).  One warp per (token, block).
-__global__ void __launch_bounds__(256) token_image_kernel(const float* __restrict__ src,
+static __global__ void __launch_bounds__(256) token_image_kernel(const float* __restrict__ src,
                                                           const uint32_t* __restrict__ tokens,
                                                           const float* __restrict__ w, uint32_t T, uint32_t K,
                                                           uint8_t* img, float* ss, float* x_out) {

@@ -501,11 +501,16 @@ constexpr uint32_t kAccBatch = 1;
 // acc += scale(row, tile) * blk[block] * y.  blk: per-block factors (null: 1).
 // Before a tile of a new row tile, flush() hands acc on (and must zero it and
 // advance cur_g).  s/ph: the ring position, carried by the caller.
-template <class Flush>
+struct NoStageHook {
+    __device__ void operator()(uint32_t, uint32_t) const {}
+};
+
+template <class Flush, class Hook = NoStageHook>
 __device__ __forceinline__ void acc_stages(uint32_t u0, uint32_t u1, uint32_t NB, uint32_t nstages, const uint8_t* ring,
                                            uint32_t NS, uint32_t taddr, uint32_t row, const float* blk,
                                            uint64_t* mma_done, uint64_t* empty, uint32_t& s, uint32_t& ph, bool& ok,
-                                           uint32_t* err, float& acc, uint32_t& cur_g, Flush flush) {
+                                           uint32_t* err, float& acc, uint32_t& cur_g, Flush flush,
+                                           Hook hook = Hook()) {
     const uint32_t lane = threadIdx.x & 31;
     uint32_t g = NB ? u0 / NB : 0, b = u0 - g * NB;  // row tile and block of the next tile
     for (uint32_t j = 0; j < nstages; j += kAccBatch) {
@@ -519,6 +524,7 @@ __device__ __forceinline__ void acc_stages(uint32_t u0, uint32_t u1, uint32_t NB
             nt[k] = 0;
             if (k < m) {
                 if (ok) ok = mbar_wait(&mma_done[s], ph, err);
+                hook(j + k, 2);
                 tcgen05_fence_after();
                 tmem_ld64(taddr + s * (kStageTiles * kTileCols), d[k]);
                 nt[k] = min(kStageTiles, u1 - (u0 + (j + k) * kStageTiles));
@@ -534,6 +540,7 @@ __device__ __forceinline__ void acc_stages(uint32_t u0, uint32_t u1, uint32_t NB
         __syncwarp();
         if (lane == 0)
             for (uint32_t k = 0; k < m; ++k) mbar_arrive(&empty[sl[k]]);  // stages (smem and TMEM columns) free
+        hook(j, 3);
 #pragma unroll
         for (uint32_t k = 0; k < kAccBatch; ++k) {
             if (k >= m) break;

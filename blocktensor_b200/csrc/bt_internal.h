@@ -15,6 +15,21 @@ struct RowMap {
     uint32_t dst_off;  // added to the mapped row
 };
 
+#ifdef __CUDACC__
+// Destination row of source row `local` of a repacked matrix.
+__device__ __forceinline__ uint32_t map_row(uint32_t local, RowMap m) {
+    const uint32_t r = local + m.src_off;
+    uint32_t d = r;
+    if (m.mode == 1) {
+        const uint32_t h = r / m.hd, i = r % m.hd, half = m.hd / 2;
+        d = h * m.hd + (i < half ? 2 * i : 2 * (i - half) + 1);
+    } else if (m.mode == 2) {
+        d = 2 * r + m.parity;
+    }
+    return d + m.dst_off;
+}
+#endif
+
 // Launchers (stream-ordered, no synchronisation).  Return cudaError_t of the launch.
 cudaError_t launch_quantize_q8_0(const float* src, void* dst, uint64_t n_blocks, cudaStream_t s);
 cudaError_t launch_dequantize_q8_0(const void* src, float* dst, uint64_t n, cudaStream_t s);
@@ -24,6 +39,9 @@ cudaError_t launch_repack_q8_0(const void* blocks, int8_t* qs, float* scales, ui
 // src_bpr: blocks per source row (0: K/32); cb0: first packed block of each source row.
 cudaError_t launch_pack_units(const void* blocks, uint8_t* units, uint32_t M, uint32_t K, RowMap map,
                               cudaStream_t s, uint32_t src_bpr = 0, uint32_t cb0 = 0);
+// The same from 20-byte Q4_0 blocks (values code - 8, bt_q4.cu).
+cudaError_t launch_pack_units_q4(const void* blocks, uint8_t* units, uint32_t M, uint32_t K, RowMap map,
+                                 cudaStream_t s, uint32_t src_bpr = 0, uint32_t cb0 = 0);
 inline uint64_t unit_bytes(uint32_t M, uint32_t K) { return (uint64_t)((M + 127) / 128) * (K / 32) * 4608; }
 cudaError_t launch_gen_normal(uint64_t seed, uint64_t stream_id, uint64_t offset, uint64_t n, float k,
                               float* out, cudaStream_t s);

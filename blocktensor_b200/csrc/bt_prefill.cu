@@ -115,8 +115,6 @@ __global__ void positions_kernel(uint32_t* pos, uint32_t T, uint32_t pos0) {
     if (t < T) pos[t] = pos0 + t;
 }
 
-namespace {
-
 template <typename KVT>
 cudaError_t launch_prefill_attn(const float* q, const KVT* kc, const KVT* vc, float* out, uint32_t T, uint32_t pos0,
                                 uint32_t H, uint32_t GQ, uint32_t hd, uint32_t max_seq, float scale, cudaStream_t s) {
@@ -159,11 +157,11 @@ int ensure_prefill_buffers(bt_engine* e) {
 }
 
 template <typename KVT>
-int prefill_chunk_t(bt_engine* e, bt_kv* kv, uint32_t T, uint32_t pos0, cudaStream_t s) {
+int prefill_chunk_t(bt_engine* e, const CacheRef& kv, uint32_t T, uint32_t pos0, cudaStream_t s) {
     const auto& c = e->lc;
     const uint32_t D = c.dim, F = c.hidden_dim, Q = qd(c), KV = kvd(c), hd = c.head_dim;
     const uint32_t QKV = Q + 2 * KV, L = c.num_layers, nsm = e->num_sms;
-    uint32_t* err = &kv->st->error;
+    uint32_t* err = kv.err;
     const float scale = 1.0f / std::sqrt((float)hd);
     positions_kernel<<<(T + 255) / 256, 256, 0, s>>>(e->pf_pos, T, pos0);
     g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -171,20 +169,20 @@ int prefill_chunk_t(bt_engine* e, bt_kv* kv, uint32_t T, uint32_t pos0, cudaStre
     // layer 0 input: the embedding rows (also the residual stream) times attn_norm
     BT_CUDA_CHECK(launch_token_image(e->embed, e->pf_tok, e->layers[0].attn_norm, T, D, e->pf_img[0], e->pf_ss,
                                      e->pf_x, s));
-    const size_t kv_layer = (size_t)c.num_kv_heads * kv->max_seq * hd;
+    const size_t kv_layer = (size_t)c.num_kv_heads * kv.max_seq * hd;
     for (uint32_t l = 0; l < L; ++l) {
         const LayerDev& Ld = e->layers[l];
-        KVT* kl = static_cast<KVT*>(kv->k) + l * kv_layer;
-        KVT* vl = static_cast<KVT*>(kv->v) + l * kv_layer;
+        KVT* kl = static_cast<KVT*>(kv.k) + l * kv_layer;
+        KVT* vl = static_cast<KVT*>(kv.v) + l * kv_layer;
         // qkv + RoPE + K/V append
         {
-            GEpiQKV<KVT> epi{e->pf_q, kl, vl, 0, kv->rope, GemmTok{T, e->pf_pos, nullptr}, Q, KV, hd, kv->max_seq};
+            GEpiQKV<KVT> epi{e->pf_q, kl, vl, 0, kv.rope, GemmTok{T, e->pf_pos, nullptr}, Q, KV, hd, kv.max_seq};
             BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.qkv, QKV, unit_rows(QKV), D},
                                              GemmIn{e->pf_img[0], e->pf_ss, c.rms_norm_eps, T}, epi, err, nsm, s));
         }
         // causal attention over the cache, then the o-proj input's token image
         BT_CUDA_CHECK(launch_prefill_attn<KVT>(e->pf_q, kl, vl, e->pf_attn, T, pos0, c.num_heads,
-                                               c.num_heads / c.num_kv_heads, hd, kv->max_seq, scale, s));
+                                               c.num_heads / c.num_kv_heads, hd, kv.max_seq, scale, s));
         BT_CUDA_CHECK(launch_token_image(e->pf_attn, nullptr, nullptr, T, Q, e->pf_img[1], nullptr, nullptr, s));
         // o-proj + residual; token image of x * ffn_norm
         BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.o, D, unit_rows(D), Q}, GemmIn{e->pf_img[1], nullptr, 0.0f, T},
@@ -204,7 +202,8 @@ int prefill_chunk_t(bt_engine* e, bt_kv* kv, uint32_t T, uint32_t pos0, cudaStre
     return BT_OK;
 }
 
-}  // namespace
+template int prefill_chunk_t<float>(bt_engine*, const CacheRef&, uint32_t, uint32_t, cudaStream_t);
+template int prefill_chunk_t<__half>(bt_engine*, const CacheRef&, uint32_t, uint32_t, cudaStream_t);
 
 cudaError_t gemm_units_launch(const void* units, const float* X, float* Y, uint32_t M, uint32_t K, uint32_t T,
                               uint8_t* img, uint32_t* err, uint32_t nsm, cudaStream_t s) {
@@ -241,8 +240,9 @@ int bt_engine_prefill(bt_engine* e, bt_kv* kv, const uint32_t* prompt, uint32_t 
     for (uint32_t done = 0; done < n_fill;) {
         const uint32_t T = std::min(n_fill - done, e->pf_cap);
         BT_CUDA_CHECK(cudaMemcpyAsync(e->pf_tok, prompt + done, sizeof(uint32_t) * T, cudaMemcpyHostToDevice, s));
-        rc = kv->dtype == BT_KV_FP16 ? prefill_chunk_t<__half>(e, kv, T, pos0 + done, s)
-                                     : prefill_chunk_t<float>(e, kv, T, pos0 + done, s);
+        const CacheRef cr{kv->k, kv->v, kv->rope, kv->max_seq, &kv->st->error};
+        rc = kv->dtype == BT_KV_FP16 ? prefill_chunk_t<__half>(e, cr, T, pos0 + done, s)
+                                     : prefill_chunk_t<float>(e, cr, T, pos0 + done, s);
         if (rc != BT_OK) return rc;
         BT_CUDA_CHECK(cudaStreamSynchronize(s));  // pf_tok is refilled from the host by the next chunk
         done += T;

@@ -65,17 +65,6 @@ __global__ void dequantize_q8_0_kernel(const uint8_t* __restrict__ src, float* _
     dst[i] = __fmul_rn(__int2float_rn(q), scale);
 }
 
-__device__ __forceinline__ uint32_t map_row(uint32_t local, RowMap m) {
-    const uint32_t r = local + m.src_off;
-    uint32_t d = r;
-    if (m.mode == 1) {
-        const uint32_t h = r / m.hd, i = r % m.hd, half = m.hd / 2;
-        d = h * m.hd + (i < half ? 2 * i : 2 * (i - half) + 1);
-    } else if (m.mode == 2) {
-        d = 2 * r + m.parity;
-    }
-    return d + m.dst_off;
-}
 
 // One thread per 32-block: 36-byte block -> 32 int8 (two 16-byte stores) + one scale.
 __global__ void repack_q8_0_kernel(const uint8_t* __restrict__ blocks, int8_t* __restrict__ qs,

@@ -93,6 +93,21 @@ enum : uint32_t {
     kTraceSlots = 8
 };
 
+// Stage timeline (a build with BT_STAGE_TRACE defined, for latency analysis):
+// after the phase part of the trace, per CTA and ring stage (the first
+// kStageTraceMax of the step): [0] the producer issues the stage's copy, [1]
+// issuer 1 sees it landed, [2] accumulator warp 5 sees its MMAs complete, [3]
+// that warp has read the results and releases the slot.
+constexpr uint32_t kStageTraceMax = 2048;
+
+__device__ __forceinline__ void stage_trace_at(const StepArgs& a, uint32_t P, uint32_t stage, uint32_t slot) {
+#ifdef BT_STAGE_TRACE
+    if (a.trace && stage < kStageTraceMax)
+        a.trace[(size_t)P * gridDim.x * kTraceSlots + ((size_t)blockIdx.x * kStageTraceMax + stage) * 4 + slot] =
+            global_ns();
+#endif
+}
+
 constexpr uint32_t kTpMaxWorld = 8;  // GPUs of one tensor parallel group
 
 enum : uint32_t { kPhQKV = 0, kPhAttn = 1, kPhO = 2, kPhGU = 3, kPhDown = 4, kPhHead = 5 };
@@ -596,6 +611,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                 }
                 uint32_t nb;
                 const uint8_t* src = cursor_src(cp, nb);
+                stage_trace_at(a, P, issued, 0);
                 mbar_expect_tx(&full[s], nb);
                 if (hint)
                     bulk_g2s_hint(ring + (size_t)s * kStageBytes, src, nb, &full[s], pol);
@@ -630,6 +646,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
     bool ok = true;
     // per-role pipeline state, carried across phases
     uint32_t rs = 0, rph = 0;              // ring slot (issuers, accumulators)
+    uint32_t rcount = 0;                   // stages passed through the ring so far
     uint32_t qs = 0, qph = 0, qn = 0;      // reduction slot (accumulators, finisher) and slots used
     uint32_t dph = 0;                      // digit-image barrier phase
     StreamState est{-INFINITY, 0xFFFFFFFFu};
@@ -695,6 +712,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                 uint32_t s = rs, ph = rph;
                 for (uint32_t j = 0; j < gm.nstages; ++j) {
                     if (ok) ok = mbar_wait(&full[s], ph, err);
+                    if (t == 0) stage_trace_at(a, P, rcount + j, 1);
                     tcgen05_fence_after();
                     if (ok) issue_stage(t, min(kStageTiles, gm.u1 - (gm.u0 + j * kStageTiles)), s, b, NB, a0, b0, d0);
                     umma_commit(&mma_done[s]);
@@ -706,6 +724,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
             // every issuer lane tracks the ring position
             for (uint32_t j = 0; j < gm.nstages; ++j)
                 if (++rs == NS) { rs = 0; rph ^= 1; }
+            rcount += gm.nstages;
             __syncwarp();
             continue;
         }
@@ -953,8 +972,16 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                 if (++qs == kRedSlots) { qs = 0; qph ^= 1; }
                 ++cur_g;
             };
+#ifdef BT_STAGE_TRACE
+            auto st_hook = [&](uint32_t j, uint32_t slot) {
+                if (warp == kAccWarp0 && lane == 0) stage_trace_at(a, P, rcount + j, slot);
+            };
+#else
+            auto st_hook = [](uint32_t, uint32_t) {};
+#endif
             acc_stages(gm.u0, gm.u1, NB, gm.nstages, ring, NS, taddr, row, blk, mma_done, empty, rs, rph, ok, err, acc,
-                       cur_g, flush);
+                       cur_g, flush, st_hook);
+            rcount += gm.nstages;
             while (cur_g <= gm.g_last) flush();
         }
     }

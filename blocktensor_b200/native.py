@@ -82,6 +82,9 @@ SIGNATURES = {
     "bt_cuda_quantize_q8_0": (_i32, [_vp, _vp, _u64, _vp]),
     "bt_cuda_dequantize_q8_0": (_i32, [_vp, _vp, _u64, _vp]),
     "bt_cuda_matvec_q8_0": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp]),
+    "bt_cuda_quantize_q4_0": (_i32, [_vp, _vp, _u64, _vp]),
+    "bt_cuda_dequantize_q4_0": (_i32, [_vp, _vp, _u64, _vp]),
+    "bt_cuda_matvec_q4_0": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp]),
     "bt_cuda_repack_q8_0": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp]),
     "bt_cuda_gemv_q8": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp]),
     "bt_cuda_gemm_q8_units": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32, _vp]),
@@ -95,6 +98,7 @@ SIGNATURES = {
     "bt_cuda_softmax": (_i32, [_vp, _vp, _u32, _u32, _vp]),
     "bt_cuda_silu": (_i32, [_vp, _vp, _u32, _vp]),
     "bt_cuda_argmax": (_i32, [_vp, _u32, _vp, _vp]),
+    "bt_cuda_sample_top_p_top_k": (_i32, [_vp, _u32, _f32, _f32, _u32, _u64, _vp, _vp]),
     "bt_engine_create": (_i32, [_i32, C.POINTER(ModelConfig), C.POINTER(EngineOptions), C.POINTER(_vp)]),
     "bt_engine_destroy": (_i32, [_vp]),
     "bt_engine_load": (_i32, [_vp, C.POINTER(TensorView), _u32, _i32]),
@@ -119,6 +123,13 @@ SIGNATURES = {
     "bt_kv_state": (_i32, [_vp, _vp, _vp, _vp]),
     "bt_kv_inject_stall": (_i32, [_vp]),
     "bt_kv_step_info": (_i32, [_vp, _u32, _vp, _vp]),
+    "bt_batch_create": (_i32, [_vp, _u32, _u32, _i32, C.POINTER(_vp)]),
+    "bt_batch_destroy": (_i32, [_vp]),
+    "bt_batch_prefill": (_i32, [_vp, _u32, _vp, _u32]),
+    "bt_batch_steps": (_i32, [_vp, _u32, _vp]),
+    "bt_batch_read_tokens": (_i32, [_vp, _u32, _u32, _u32, _vp]),
+    "bt_batch_read_logits": (_i32, [_vp, _vp]),
+    "bt_batch_step_info": (_i32, [_vp, _vp]),
 }
 
 _LIB = None

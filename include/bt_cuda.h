@@ -93,6 +93,7 @@ typedef struct bt_tensor_view {
 
 typedef struct bt_engine bt_engine;
 typedef struct bt_kv bt_kv;
+typedef struct bt_batch bt_batch;
 
 /* ------------------------------------------------------------------ */
 /* Library                                                              */
@@ -131,6 +132,18 @@ BT_API int bt_cuda_quantize_q8_0(const float* src, void* dst_blocks, uint64_t n,
 
 /* Replaces quantization::dequantize_q8_0 (quant_types.cpp:36-48, decl. quant_types.hpp:23). */
 BT_API int bt_cuda_dequantize_q8_0(const void* src_blocks, float* dst, uint64_t n, void* stream);
+
+/* Replaces quantization::quantize_q4_0 (quant_types.cpp:50-79, decl.
+ * quant_types.hpp:25): dst gets n/32 BlockQ4_0 of 20 bytes (fp32 scale, then
+ * 16 bytes of 4-bit codes, element 2i in the low nibble of byte i).  Bit-exact
+ * with the reference for finite inputs; n % 32 != 0 -> BT_ERR_INVALID_ARGUMENT. */
+BT_API int bt_cuda_quantize_q4_0(const float* src, void* dst_blocks, uint64_t n, void* stream);
+/* Replaces quantization::dequantize_q4_0 (quant_types.cpp:81-99, decl. quant_types.hpp:26). */
+BT_API int bt_cuda_dequantize_q4_0(const void* src_blocks, float* dst, uint64_t n, void* stream);
+/* Replaces quantization::matvec_q4_0 (quant_types.cpp:123-147, decl.
+ * quant_types.hpp:29) and the "matvec_q4_0" pipeline (transformer_engine.cpp:63-65,
+ * 87-91): Y[M] = W[M x N] X[N], W in the reference's 20-byte block layout. */
+BT_API int bt_cuda_matvec_q4_0(const void* W_blocks, const float* X, float* Y, uint32_t M, uint32_t N, void* stream);
 
 /* Replaces quantization::matvec_q8_0 (quant_types.cpp:101-121, decl.
  * quant_types.hpp:28) and the "matvec_q8_0" pipeline of the Vulkan backend
@@ -241,6 +254,16 @@ BT_API int bt_cuda_softmax(const float* in, float* out, uint32_t rows, uint32_t 
 BT_API int bt_cuda_silu(const float* in, float* out, uint32_t n, void* stream);
 /* sampling::sample_greedy (sampler.hpp:11-13): first maximum wins. out: device uint32. */
 BT_API int bt_cuda_argmax(const float* logits, uint32_t n, uint32_t* out, void* stream);
+/* sampling::sample_top_p_top_k (sampler.hpp:15-85) on the device: logits
+ * [vocab] divided by the temperature, the top_k largest kept in decreasing
+ * order, probabilities exp(l - max) / sum, cut where the running sum reaches
+ * top_p, renormalised, and the token where the running sum first reaches r, r
+ * the first std::uniform_real_distribution<float>(0, 1) draw of
+ * std::mt19937(seed) (computed on the host as the reference does).
+ * temperature <= 0: greedy.  Candidates: top_k in 1..4096 (or all of a vocab
+ * of at most 4096); equal logits are ordered by id.  out: device uint32. */
+BT_API int bt_cuda_sample_top_p_top_k(const float* logits, uint32_t vocab, float temperature, float top_p,
+                                      uint32_t top_k, uint64_t seed, uint32_t* out, void* stream);
 
 /* ------------------------------------------------------------------ */
 /* Engine (runtime/include/blocktensor/transformer_engine.hpp:12-56)    */
@@ -259,7 +282,10 @@ BT_API int bt_engine_destroy(bt_engine* e);
  * (models/model_importer.cpp:69-85: embed, out_norm, head, then per layer
  * attn_norm, ffn_norm, q, k, v, o, gate, up, down).  on_device = 0: host
  * pointers (importer output, IComputeBuffer::map of HOST_VISIBLE buffers);
- * on_device = 1: device pointers.  Matrices are repacked on the device. */
+ * on_device = 1: device pointers.  Matrices are Q8_0 (36-byte blocks) or, for
+ * an INT4 model, Q4_0 (20-byte blocks; told apart by the head's size), and are
+ * repacked on the device into int8 tiles (Q4_0 codes as code - 8 with the
+ * block scale, the values matvec_q4_0 multiplies). */
 BT_API int bt_engine_load(bt_engine* e, const bt_tensor_view* tensors, uint32_t n_tensors, int on_device);
 
 /* Seeded synthetic weights generated on the device: matrices
@@ -372,6 +398,36 @@ BT_API int bt_kv_inject_stall(bt_kv* kv);
  * when the step processes position context-1: weights (int8 + fp32 scales),
  * norms, one embedding row, KV read of `context` positions and the KV write. */
 BT_API int bt_kv_step_info(bt_kv* kv, uint32_t context, uint64_t* launches, uint64_t* bytes);
+
+/* ------------------------------------------------------------------ */
+/* Batched decode (no reference counterpart: the reference KVCache holds one */
+/* sequence, runtime/src/kv_cache.cpp:6-15; a batch of n sequences is n     */
+/* independent forward_single_token loops, decoded here in one pass)        */
+/* ------------------------------------------------------------------ */
+
+/* n_seq sequences of up to max_seq positions each (KV caches fp32 or fp16) on
+ * the engine's device.  Each step processes every sequence's current token at
+ * its own position: the projections as tensor-core GEMMs over the batch (the
+ * weights stream once per step), attention per sequence over its own cache,
+ * the head with a greedy argmax per sequence.  No tensor parallelism; shard
+ * sequences over GPUs by giving each GPU its own engine and batch. */
+BT_API int bt_batch_create(bt_engine* e, uint32_t n_seq, uint32_t max_seq, int kv_dtype, bt_batch** out);
+BT_API int bt_batch_destroy(bt_batch* b);
+/* Sequence s starts with `prompt`: positions 0 .. n_prompt - 2 are prefilled
+ * (as bt_engine_prefill), and its next step processes prompt[n_prompt - 1] at
+ * position n_prompt - 1.  Every sequence must be started before steps run. */
+BT_API int bt_batch_prefill(bt_batch* b, uint32_t s, const uint32_t* prompt, uint32_t n_prompt);
+/* n decode steps of every sequence (greedy), on `stream` (NULL: the engine's);
+ * BT_ERR_OUT_OF_RANGE when a sequence would pass max_seq. */
+BT_API int bt_batch_steps(bt_batch* b, uint32_t n, void* stream);
+/* Token consumed by sequence s at positions pos0 .. pos0 + n - 1 (prompt, then
+ * greedy tokens); BT_ERR_DEVICE_TIMEOUT when a device wait gave up. */
+BT_API int bt_batch_read_tokens(bt_batch* b, uint32_t s, uint32_t pos0, uint32_t n, uint32_t* out);
+/* Logits of every sequence's last step, [n_seq][vocab] fp32 (host). */
+BT_API int bt_batch_read_logits(bt_batch* b, float* out);
+/* Algorithmic HBM bytes of the next step: weights once, norms, one embedding
+ * row per sequence, every sequence's K/V read and written. */
+BT_API int bt_batch_step_info(bt_batch* b, uint64_t* bytes);
 
 #ifdef __cplusplus
 }

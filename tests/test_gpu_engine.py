@@ -243,3 +243,45 @@ def test_device_wait_expiry_reports_timeout(cuda, tiny):
     again = eng.decode(kv, prompt, n_gen=8)  # begin() resets the state and its error flag
     assert list(again) == list(clean)
     kv.state()
+
+
+def test_btmodel_v2_from_converter_drives_engine(cuda, oracle, ref, tmp_path):
+    """A safetensors checkpoint converted to .btmodel v2 loads into the CUDA engine and
+    matches the reference engine on the same tensors (its v1 copy)."""
+    import json
+    from blocktensor_b200 import btmodel, convert
+    D, F, L, H, KVH, V = 128, 256, 2, 4, 2, 512
+    rng = np.random.default_rng(3)
+    t = {"model.embed_tokens.weight": rng.standard_normal((V, D)) * 0.02, "model.norm.weight": np.ones(D)}
+    for l in range(L):
+        p = f"model.layers.{l}."
+        t[p + "input_layernorm.weight"] = np.ones(D)
+        t[p + "post_attention_layernorm.weight"] = np.ones(D)
+        for n, shape in (("self_attn.q_proj", (D, D)), ("self_attn.k_proj", (KVH * 32, D)),
+                         ("self_attn.v_proj", (KVH * 32, D)), ("self_attn.o_proj", (D, D)),
+                         ("mlp.gate_proj", (F, D)), ("mlp.up_proj", (F, D)), ("mlp.down_proj", (D, F))):
+            t[p + n + ".weight"] = rng.standard_normal(shape) * 0.05
+    d = tmp_path / "ckpt"
+    d.mkdir()
+    convert.write_safetensors(str(d / "model.safetensors"), t)
+    json.dump({"hidden_size": D, "intermediate_size": F, "num_hidden_layers": L, "num_attention_heads": H,
+               "num_key_value_heads": KVH, "vocab_size": V, "rope_theta": 10000.0,
+               "max_position_embeddings": 64}, open(d / "config.json", "w"))
+    out = str(tmp_path / "m.btmodel")
+    convert.convert(str(d), out, kv_dtype="fp32")
+    eng = cuda.TransformerEngine.from_btmodel(out)
+    m = btmodel.read_btmodel_v2(out)
+    v1 = str(tmp_path / "m1.btmodel")
+    btmodel.write_btmodel(v1, m.config, m.tensors)
+    r = oracle.RefEngine.from_file(ref, v1, kv_max_seq=64)
+    kv = cuda.KVCache(eng, 64)
+    tok = 7
+    for p in range(24):
+        a = eng.forward_single_token(tok, p, kv)
+        b = r.forward(tok, p)
+        assert_close_act(a, b, f"pos {p}")
+        assert int(np.argmax(a)) == int(np.argmax(b))
+        tok = int(np.argmax(b))
+    r.close()
+    kv.close()
+    eng.close()
