@@ -358,11 +358,18 @@ class Batch:
     """Independent sequences decoded together (bt_batch_*): one token row per sequence in
     every tensor-core GEMM, attention per sequence over its own cache."""
 
-    def __init__(self, engine: TransformerEngine, n_seq: int, max_seq: int, kv_dtype: int = BT_KV_FP32):
+    def __init__(self, engine: TransformerEngine, n_seq: int, max_seq: int, kv_dtype: int = BT_KV_FP32,
+                 page_tokens: int = 0, n_pages: int = 0):
+        """page_tokens > 0: the KV lives in a pool of n_pages pages of page_tokens positions
+        (bt_batch_create_paged) that the sequences take as they grow and give back on release()."""
         self.engine = engine
         self.n_seq, self.max_seq = n_seq, max_seq
+        self.page_tokens, self.n_pages = page_tokens, n_pages
         h = C.c_void_p()
-        call("bt_batch_create", engine.handle, n_seq, max_seq, kv_dtype, C.byref(h))
+        if page_tokens:
+            call("bt_batch_create_paged", engine.handle, n_seq, max_seq, page_tokens, n_pages, kv_dtype, C.byref(h))
+        else:
+            call("bt_batch_create", engine.handle, n_seq, max_seq, kv_dtype, C.byref(h))
         self._h = h
 
     def close(self):
@@ -397,6 +404,16 @@ class Batch:
         b = C.c_uint64()
         call("bt_batch_step_info", self._h, C.byref(b))
         return b.value
+
+    def release(self, s: int):
+        """Ends slot s's sequence: its pages go back to the pool (paged batches only)."""
+        call("bt_batch_release", self._h, s)
+
+    def pages(self):
+        """(free, total) pages of the pool."""
+        f, t = C.c_uint32(), C.c_uint32()
+        call("bt_batch_pages", self._h, C.byref(f), C.byref(t))
+        return f.value, t.value
 
 
 class KVCache:

@@ -17,7 +17,7 @@ CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libbt_cuda.so")
 
 SOURCES = ["bt_quant.cu", "bt_prims.cu", "bt_engine.cu", "bt_noalloc.cu", "bt_prefill.cu", "bt_batch.cu", "bt_q4.cu", "bt_sample.cu"]
-HEADERS = ["bt_common.cuh", "bt_gemv.cuh", "bt_gemv_mma.cuh", "bt_ptx.cuh", "bt_attention.cuh", "bt_step.cuh",
+HEADERS = ["bt_attn_mma.cuh", "bt_common.cuh", "bt_gemv.cuh", "bt_gemv_mma.cuh", "bt_ptx.cuh", "bt_attention.cuh", "bt_step.cuh",
            "bt_gemm.cuh", "bt_engine_impl.h", "bt_internal.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -39,13 +39,15 @@ def _stale(target: str, deps: list[str]) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force: bool = False, verbose_ptxas: bool = False, jobs: int = 0) -> str:
+def build(force: bool = False, verbose_ptxas: bool = False, jobs: int = 0, defines: tuple = ()) -> str:
+    """defines: extra preprocessor symbols, e.g. BT_STAGE_TRACE for the step kernel's per-stage
+    timeline (a diagnostic build; build it in a copy of the package)."""
     deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS] + [os.path.join(ROOT, "include", "bt_cuda.h")]
-    if not force and not _stale(LIB, deps):
+    if not force and not defines and not _stale(LIB, deps):
         return LIB
     objdir = os.path.join(PKG, "_build")
     os.makedirs(objdir, exist_ok=True)
-    extra = ["-Xptxas", "-v"] if verbose_ptxas else []
+    extra = (["-Xptxas", "-v"] if verbose_ptxas else []) + [f"-D{d}" for d in defines]
     procs = []
     objs = []
     for src in SOURCES:
@@ -74,5 +76,6 @@ if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--ptxas-v", action="store_true")
+    ap.add_argument("--define", action="append", default=[], help="preprocessor symbol (e.g. BT_STAGE_TRACE)")
     a = ap.parse_args()
-    print(build(force=a.force, verbose_ptxas=a.ptxas_v))
+    print(build(force=a.force, verbose_ptxas=a.ptxas_v, defines=tuple(a.define)))

@@ -57,17 +57,43 @@ CudaTransformerEngine::CudaTransformerEngine(std::shared_ptr<IComputeBackend> ba
 }
 
 CudaTransformerEngine::~CudaTransformerEngine() {
-    for (auto& kv : kvs_) bt_kv_destroy(kv.second);
+    for (auto& kv : kvs_) bt_kv_destroy(kv.second.h);
     bt_engine_destroy(eng_);
 }
 
 bt_kv* CudaTransformerEngine::kv_for(const KVCache& kv) {
+    if (cfg_.num_layers == 0) throw std::invalid_argument("CudaTransformerEngine: model without layers");
+    const std::shared_ptr<IComputeBuffer> k0 = kv.k_cache(0);
     auto it = kvs_.find(&kv);
-    if (it != kvs_.end()) return it->second;
+    if (it != kvs_.end()) {
+        if (it->second.k0.lock() == k0) return it->second.h;
+        bt_kv_destroy(it->second.h);  // a destroyed KVCache's address, reused by a new one
+        kvs_.erase(it);
+    }
+    // device caches of KVCaches that no longer exist
+    for (auto i = kvs_.begin(); i != kvs_.end();) {
+        if (i->second.k0.expired()) {
+            bt_kv_destroy(i->second.h);
+            i = kvs_.erase(i);
+        } else {
+            ++i;
+        }
+    }
     bt_kv* h = nullptr;
     bt_throw_if_error(bt_kv_create(eng_, kv.max_seq_len(), kv_dtype_, &h), "bt_kv_create");
-    kvs_[&kv] = h;
+    kvs_[&kv] = KvBinding{k0, h};
     return h;
+}
+
+void CudaTransformerEngine::sync_to_reference(KVCache& kv_cache) {
+    bt_kv* h = kv_for(kv_cache);
+    const size_t n = (size_t)kv_cache.max_seq_len() * cfg_.num_kv_heads * cfg_.head_dim;
+    std::vector<float> k(n), v(n);
+    for (uint32_t l = 0; l < cfg_.num_layers; ++l) {
+        bt_throw_if_error(bt_kv_read_layer(h, l, k.data(), v.data()), "bt_kv_read_layer");
+        kv_cache.k_cache(l)->write(k.data(), n * sizeof(float), 0);
+        kv_cache.v_cache(l)->write(v.data(), n * sizeof(float), 0);
+    }
 }
 
 std::vector<float> CudaTransformerEngine::forward_single_token(uint32_t token_id, uint32_t pos, KVCache& kv_cache) {

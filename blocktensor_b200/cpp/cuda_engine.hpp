@@ -9,7 +9,12 @@
 // from the TransformerWeights buffers: CudaBuffers are loaded device-to-device,
 // any other buffers are read to the host first.  Each KVCache object seen is
 // paired with a device cache of the same max_seq_len (fp32 by default, as
-// runtime/src/kv_cache.cpp:9).
+// runtime/src/kv_cache.cpp:9).  The pairing is by the identity of the
+// KVCache's buffers (it holds them; they die with it), so a new KVCache that
+// happens to reuse a destroyed one's address gets a fresh device cache.  The
+// device cache is the one the kernels read and write; sync_to_reference copies
+// it into the KVCache's own buffers for callers that read K/V through the
+// reference object (k_cache / v_cache).
 #pragma once
 
 #include <cstdint>
@@ -34,6 +39,10 @@ public:
 
     std::vector<float> forward_single_token(uint32_t token_id, uint32_t pos, KVCache& kv_cache);
 
+    // Copies the device K/V of kv_cache's sequence into its reference buffers, layout
+    // [max_seq][kv_heads][head_dim] fp32 per layer (runtime/src/kv_cache.cpp:21-23).
+    void sync_to_reference(KVCache& kv_cache);
+
     // Greedy token of the last forward_single_token (sampling::sample_greedy of its logits).
     uint32_t last_argmax() const { return last_argmax_; }
     bt_engine* handle() const { return eng_; }
@@ -46,7 +55,11 @@ private:
     int device_ = 0;
     int kv_dtype_;
     bt_engine* eng_ = nullptr;
-    std::unordered_map<const KVCache*, bt_kv*> kvs_;
+    struct KvBinding {
+        std::weak_ptr<IComputeBuffer> k0;  // the KVCache's layer-0 K buffer: expires with the KVCache
+        bt_kv* h = nullptr;
+    };
+    std::unordered_map<const KVCache*, KvBinding> kvs_;
     uint32_t last_argmax_ = 0;
 };
 

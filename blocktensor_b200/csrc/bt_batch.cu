@@ -16,6 +16,7 @@
 //   gate/up GEMM : silu(gate) * up                                      (:197-215)
 //   down GEMM    : x += down                                            (:217-225)
 //   head GEMM    : logits and a per-32-row argmax, reduced per sequence  (:244-250, sampler.hpp:11-13)
+#include "bt_attn_mma.cuh"
 #include "bt_common.cuh"
 #include "bt_gemm.cuh"
 #include "bt_step.cuh"
@@ -35,9 +36,19 @@ struct bt_batch {
     uint32_t n_seq = 0, max_seq = 0;
     int dtype = BT_KV_FP32;
     std::vector<void*> allocs;
-    void* k = nullptr;           // [n_seq][L][KVH][max_seq][hd]
+    void* k = nullptr;           // contiguous: [n_seq][L][KVH][max_seq][hd]; paged: [n_pages][L][KVH][P][hd]
     void* v = nullptr;
-    size_t seq_stride = 0;       // elements between two sequences' caches
+    size_t seq_stride = 0;       // contiguous: elements between two sequences' caches
+    size_t layer_stride = 0;     // elements between two layers' bases (per sequence, or inside a page)
+    KVMap map;                   // row addresses (the table pointer set when paged)
+    // paged KV: a pool of n_pages pages of 2^page_shift positions shared by the sequences;
+    // table[s][j] = the page holding positions j P .. j P + P - 1 of sequence s
+    bool paged = false;
+    uint32_t page_shift = 0, n_pages = 0, max_pages = 0;
+    uint32_t* table = nullptr;              // device [n_seq][max_pages]
+    std::vector<uint32_t> host_table;       // its host copy (kNoPage: none)
+    std::vector<uint32_t> free_pages;       // pages no sequence holds (taken from the back)
+    std::vector<uint32_t> seq_pages;        // pages held per sequence
     float2* rope = nullptr;      // [max_seq][hd/2]
     uint32_t* pos = nullptr;     // [n_seq] position of the token the next step processes
     uint32_t* cur = nullptr;     // [n_seq] the token it consumes
@@ -55,6 +66,8 @@ struct bt_batch {
     uint8_t* img[2] = {nullptr, nullptr};
     float* att_part = nullptr;   // [n_seq][KVH][S][GQ][hd + 2]
     uint32_t S = 1, kps = 1;     // attention splits, keys per split
+    float* gpart = nullptr;      // split-K partial sums of the GEMMs with fewer units than SMs
+    size_t gpart_floats = 0;
     float* am_val = nullptr;     // [n_seq][Mp(V) / 32]
     uint32_t* am_idx = nullptr;
     std::vector<uint32_t> host_pos;
@@ -131,11 +144,37 @@ __global__ void batch_finish_kernel(const float* __restrict__ pv, const uint32_t
 // batches of 8 (all loads in flight), online softmax per query head, lane i
 // holding head dims NV i .. NV i + NV - 1; the warps' (m, l, o) are merged in
 // shared memory and the split's written to part (l = 0: no keys).
+// The CTA's partial of a split: its 8 warps' (m, l, o) [8][GQ][HD + 2] in shared
+// memory merged (empty warps, l = 0, skipped) into out[GQ][HD + 2].
+__device__ __forceinline__ void cta_merge_partials(const float* wm, float* out, uint32_t GQ, uint32_t HD) {
+    const uint32_t pstride = HD + 2;
+    for (uint32_t e = threadIdx.x; e < GQ * HD; e += blockDim.x) {
+        const uint32_t g = e / HD, d = e % HD;
+        float M = -INFINITY;
+        for (uint32_t ww = 0; ww < 8; ++ww) {
+            const float* p = wm + ((size_t)ww * GQ + g) * pstride;
+            if (p[1] > 0.0f) M = fmaxf(M, p[0]);
+        }
+        float lsum = 0.0f, acc = 0.0f;
+        for (uint32_t ww = 0; ww < 8; ++ww) {
+            const float* p = wm + ((size_t)ww * GQ + g) * pstride;
+            if (p[1] > 0.0f) {
+                const float f = expf(p[0] - M);
+                lsum = fmaf(p[1], f, lsum);
+                acc = fmaf(p[2 + d], f, acc);
+            }
+        }
+        float* po = out + (size_t)g * pstride;
+        po[2 + d] = acc;
+        if (d == 0) { po[0] = M; po[1] = lsum; }
+    }
+}
+
 struct BatchAttnArgs {
     const float* q;          // [B][DQ]
-    const void* kc;          // this layer's cache of sequence 0
+    const void* kc;          // this layer's K base (row addresses from map)
     const void* vc;
-    size_t seq_stride;       // elements between sequences
+    KVMap map;
     const uint32_t* pos;     // [B]
     float* part;             // [B][KVH][S][GQ][hd + 2]
     uint32_t S, kps, KVH, GQ, hd, max_seq;
@@ -160,8 +199,8 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(BatchAttnArgs a) {
         }
         return;
     }
-    const KVT* kb = static_cast<const KVT*>(a.kc) + (size_t)s * a.seq_stride + (size_t)kvh * a.max_seq * HD;
-    const KVT* vb = static_cast<const KVT*>(a.vc) + (size_t)s * a.seq_stride + (size_t)kvh * a.max_seq * HD;
+    const KVT* kc = static_cast<const KVT*>(a.kc);
+    const KVT* vc = static_cast<const KVT*>(a.vc);
     const uint32_t d0 = lane * NV;
     const bool active = d0 < HD;
     const size_t DQ = (size_t)a.KVH * GQ * HD;
@@ -183,8 +222,9 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(BatchAttnArgs a) {
             for (int j = 0; j < B; ++j) {
                 const uint32_t t = base + j * 8;
                 if (t < t1 && active) {
-                    kr[j].load(kb + (size_t)t * HD + d0);
-                    vr[j].load(vb + (size_t)t * HD + d0);
+                    const size_t ro = a.map.row(s, kvh, t) + d0;
+                    kr[j].load(kc + ro);
+                    vr[j].load(vc + ro);
                 } else {
                     kr[j].zero();
                     vr[j].zero();
@@ -232,31 +272,56 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(BatchAttnArgs a) {
         }
     }
     __syncthreads();
-    // the CTA's partial of this split: the 8 warps' (m, l, o) merged
-    for (uint32_t e = threadIdx.x; e < GQ * HD; e += blockDim.x) {
-        const uint32_t g = e / HD, d = e % HD;
-        float M = -INFINITY;
-        for (uint32_t ww = 0; ww < 8; ++ww) {
-            const float* p = wm + ((size_t)ww * GQ + g) * pstride;
-            if (p[1] > 0.0f) M = fmaxf(M, p[0]);
-        }
-        float lsum = 0.0f, acc = 0.0f;
-        for (uint32_t ww = 0; ww < 8; ++ww) {
-            const float* p = wm + ((size_t)ww * GQ + g) * pstride;
-            if (p[1] > 0.0f) {
-                const float f = expf(p[0] - M);
-                lsum = fmaf(p[1], f, lsum);
-                acc = fmaf(p[2 + d], f, acc);
-            }
-        }
-        float* po = out + (size_t)g * pstride;
-        po[2 + d] = acc;
-        if (d == 0) { po[0] = M; po[1] = lsum; }
-    }
+    cta_merge_partials(wm, out, GQ, HD);
 }
 
-// attn[s][h hd + d] from the splits of (s, kv head, query head), in split order with
-// online rescaling.  One warp per (sequence, query head).
+// Tensor-core variant (bt_attn_mma.cuh) for up to 8 query heads per KV head:
+// warps take 16-key tiles of the split round robin.
+template <int HD, typename KVT>
+__global__ void __launch_bounds__(256, (HD == 64 && sizeof(KVT) == 2) ? 2 : 1) batch_attn_mma_kernel(BatchAttnArgs a) {
+    extern __shared__ float wm[];  // [8 warps][GQ][HD + 2]
+    const uint32_t lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const uint32_t sp = blockIdx.x, kvh = blockIdx.y, s = blockIdx.z;
+    const uint32_t GQ = a.GQ, pstride = HD + 2;
+    const uint32_t c = min(a.pos[s] + 1, a.max_seq);
+    const uint32_t t0 = sp * a.kps, t1 = min(c, t0 + a.kps);
+    float* out = a.part + ((((size_t)s * a.KVH + kvh) * a.S + sp) * GQ) * pstride;
+    if (t0 >= t1) {
+        for (uint32_t g = threadIdx.x; g < GQ; g += blockDim.x) {
+            out[(size_t)g * pstride] = -INFINITY;
+            out[(size_t)g * pstride + 1] = 0.0f;
+        }
+        return;
+    }
+    const KVT* kc = static_cast<const KVT*>(a.kc);
+    const KVT* vc = static_cast<const KVT*>(a.vc);
+    const size_t DQ = (size_t)a.KVH * GQ * HD;
+    // q's fragments once for the 8 warps, after their partials
+    using GW = GqaWarp<HD, KVT, true>;
+    uint4* qs = reinterpret_cast<uint4*>(wm + ((size_t)8 * GQ * pstride + 3) / 4 * 4);
+    GW::stage_q(qs, a.q + (size_t)s * DQ + (size_t)kvh * GQ * HD, GQ, threadIdx.x, blockDim.x);
+    __syncthreads();
+    GW st;
+    st.init(nullptr, GQ, lane, qs);
+    const KVMap map = a.map;
+    auto row = [&](uint32_t t) { return map.row(s, kvh, t); };
+    // the warp's tiles k0, k0 + 128, ...: the next tile's rows load while this one computes
+    uint32_t k0 = t0 + 16 * w;
+    typename GW::Tile cur, nxt;
+    if (k0 < t1) st.load(cur, kc, vc, k0, t1, row);
+    for (; k0 < t1; k0 += 16 * 8) {
+        if (k0 + 16 * 8 < t1) st.load(nxt, kc, vc, k0 + 16 * 8, t1, row);
+        st.compute(cur, k0, t1, a.scale);
+        cur = nxt;
+    }
+    st.store(wm + (size_t)w * GQ * pstride, GQ);
+    __syncthreads();
+    cta_merge_partials(wm, out, GQ, HD);
+}
+
+// attn[s][h hd + d] from the splits of (s, kv head, query head): the splits'
+// maxima and sums first (lane i holds split i, i + 32, ...), then o as the
+// weighted sum over the splits in split order.  One warp per (sequence, query head).
 __global__ void batch_attn_merge_kernel(const float* __restrict__ part, float* __restrict__ attn, uint32_t B,
                                         uint32_t KVH, uint32_t GQ, uint32_t S, uint32_t hd) {
     const uint32_t lane = threadIdx.x & 31;
@@ -265,24 +330,43 @@ __global__ void batch_attn_merge_kernel(const float* __restrict__ part, float* _
     if (item >= B * H) return;
     const uint32_t s = item / H, h = item % H, kvh = h / GQ, g = h % GQ;
     const uint32_t pstride = hd + 2;
+    const float* base = part + (((size_t)s * KVH + kvh) * S * GQ + g) * pstride;  // split sp at + sp GQ pstride
+    const size_t sstride = (size_t)GQ * pstride;
+    float M = -INFINITY;
+    for (uint32_t sp = lane; sp < S; sp += 32) {
+        const float* p = base + sp * sstride;
+        if (__ldg(p + 1) > 0.0f) M = fmaxf(M, __ldg(p));
+    }
+    M = warp_max(M);
+    float L = 0.0f;
+    for (uint32_t sp = lane; sp < S; sp += 32) {
+        const float* p = base + sp * sstride;
+        const float ls = __ldg(p + 1);
+        if (ls > 0.0f) L = fmaf(ls, expf(__ldg(p) - M), L);
+    }
+    L = warp_sum(L);
     for (uint32_t d = lane; d < hd; d += 32) {
-        float Mr = -INFINITY, lr = 0.0f, ar = 0.0f;
-        for (uint32_t sp = 0; sp < S; ++sp) {
-            const float* p = part + ((((size_t)s * KVH + kvh) * S + sp) * GQ + g) * pstride;
-            const float ms = p[0], ls = p[1], os = p[2 + d];
-            if (!(ls > 0.0f)) continue;
-            if (ms > Mr) {
-                const float r = expf(Mr - ms);
-                lr = fmaf(lr, r, ls);
-                ar = fmaf(ar, r, os);
-                Mr = ms;
-            } else {
-                const float f = expf(ms - Mr);
-                lr = fmaf(ls, f, lr);
-                ar = fmaf(os, f, ar);
+        float acc = 0.0f;
+        for (uint32_t sp0 = 0; sp0 < S; sp0 += 8) {
+            float ov[8], wv[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const uint32_t sp = sp0 + k;
+                ov[k] = 0.0f;
+                wv[k] = 0.0f;
+                if (sp < S) {
+                    const float* p = base + sp * sstride;
+                    const float ls = __ldg(p + 1);
+                    if (ls > 0.0f) {
+                        wv[k] = expf(__ldg(p) - M);
+                        ov[k] = __ldg(p + 2 + d);
+                    }
+                }
             }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc = fmaf(ov[k], wv[k], acc);
         }
-        attn[(size_t)s * H * hd + (size_t)h * hd + d] = __fdiv_rn(ar, lr);
+        attn[(size_t)s * H * hd + (size_t)h * hd + d] = __fdiv_rn(acc, L);
     }
 }
 
@@ -301,8 +385,25 @@ cudaError_t launch_batch_attn_t(const BatchAttnArgs& a, uint32_t B, cudaStream_t
     return cudaGetLastError();
 }
 
+template <int HD, typename KVT>
+cudaError_t launch_batch_attn_mma(const BatchAttnArgs& a, uint32_t B, cudaStream_t st) {
+    // the warps' partials, then q's fragments (16 bytes per lane and k-step)
+    const size_t smem = ((size_t)8 * a.GQ * (HD + 2) + 3) / 4 * 4 * sizeof(float) + (size_t)32 * (HD / 8) * 16;
+    auto kern = batch_attn_mma_kernel<HD, KVT>;
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    kern<<<dim3(a.S, a.KVH, B), 256, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
 template <typename KVT>
 cudaError_t launch_batch_attn(const BatchAttnArgs& a, uint32_t B, cudaStream_t st) {
+    // the tensor-core kernel for head_dim 64 / 128 and up to 8 query heads per KV head
+    if (a.GQ <= 8 && a.hd == 64) return launch_batch_attn_mma<64, KVT>(a, B, st);
+    if (a.GQ <= 8 && a.hd == 128) return launch_batch_attn_mma<128, KVT>(a, B, st);
     const bool mha = a.GQ == 1;
 #define BT_BATCH_ATTN(NV_)                                                                               \
     return mha ? launch_batch_attn_t<NV_, 1, KVT>(a, B, st) : launch_batch_attn_t<NV_, 16 / NV_, KVT>(a, B, st)
@@ -320,18 +421,24 @@ int enqueue_batch_step(bt_batch* b, cudaStream_t s) {
     const uint32_t QKV = Q + 2 * KV, L = c.num_layers, nsm = e->num_sms, B = b->n_seq;
     const uint32_t GQ = c.num_heads / c.num_kv_heads;
     uint32_t* err = b->err;
+    // GEMM inputs with the split-K workspace (used when a GEMM has fewer units than SMs)
+    auto gin = [&](const uint8_t* img, const float* ss, float eps) {
+        GemmIn g{img, ss, eps, B};
+        g.part = b->gpart;
+        g.part_floats = b->gpart_floats;
+        return g;
+    };
     BT_CUDA_CHECK(launch_token_image(e->embed, b->cur, e->layers[0].attn_norm, B, D, b->img[0], b->ss, b->x, s));
-    const size_t kv_layer = (size_t)c.num_kv_heads * b->max_seq * hd;
     for (uint32_t l = 0; l < L; ++l) {
         const LayerDev& Ld = e->layers[l];
-        KVT* kl = static_cast<KVT*>(b->k) + l * kv_layer;
-        KVT* vl = static_cast<KVT*>(b->v) + l * kv_layer;
+        KVT* kl = static_cast<KVT*>(b->k) + l * b->layer_stride;
+        KVT* vl = static_cast<KVT*>(b->v) + l * b->layer_stride;
         {
-            GEpiQKV<KVT> epi{b->q, kl, vl, b->seq_stride, b->rope, GemmTok{B, b->pos, b->seq_idx}, Q, KV, hd, b->max_seq};
-            BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.qkv, QKV, unit_rows(QKV), D},
-                                             GemmIn{b->img[0], b->ss, c.rms_norm_eps, B}, epi, err, nsm, s));
+            GEpiQKV<KVT> epi{b->q, kl, vl, b->map, b->rope, GemmTok{B, b->pos, b->seq_idx}, Q, KV, hd};
+            BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.qkv, QKV, unit_rows(QKV), D}, gin(b->img[0], b->ss, c.rms_norm_eps),
+                                             epi, err, nsm, s));
         }
-        BatchAttnArgs aa{b->q, kl, vl, b->seq_stride, b->pos, b->att_part, b->S, b->kps, c.num_kv_heads, GQ, hd,
+        BatchAttnArgs aa{b->q, kl, vl, b->map, b->pos, b->att_part, b->S, b->kps, c.num_kv_heads, GQ, hd,
                          b->max_seq, 1.0f / std::sqrt((float)hd)};
         BT_CUDA_CHECK(launch_batch_attn<KVT>(aa, B, s));
         {
@@ -342,17 +449,16 @@ int enqueue_batch_step(bt_batch* b, cudaStream_t s) {
             BT_CUDA_CHECK(cudaGetLastError());
         }
         BT_CUDA_CHECK(launch_token_image(b->attn, nullptr, nullptr, B, Q, b->img[1], nullptr, nullptr, s));
-        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.o, D, unit_rows(D), Q}, GemmIn{b->img[1], nullptr, 0.0f, B},
+        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.o, D, unit_rows(D), Q}, gin(b->img[1], nullptr, 0.0f),
                                          GEpiResidual{b->x, Ld.ffn_norm, b->img[0], b->ss, nullptr, D}, err, nsm, s));
-        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.gu, 2 * F, unit_rows(2 * F), D},
-                                         GemmIn{b->img[0], b->ss, c.rms_norm_eps, B},
+        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.gu, 2 * F, unit_rows(2 * F), D}, gin(b->img[0], b->ss, c.rms_norm_eps),
                                          GEpiSwiGLU{b->act, b->img[1], F}, err, nsm, s));
         const float* wn = l + 1 < L ? e->layers[l + 1].attn_norm : e->out_norm;
-        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.d, D, unit_rows(D), F}, GemmIn{b->img[1], nullptr, 0.0f, B},
+        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.d, D, unit_rows(D), F}, gin(b->img[1], nullptr, 0.0f),
                                          GEpiResidual{b->x, wn, b->img[0], b->ss, nullptr, D}, err, nsm, s));
     }
     const uint32_t nob = unit_rows(V) / 32;
-    BT_CUDA_CHECK(launch_gemm_digits(UnitW{e->head, V, unit_rows(V), D}, GemmIn{b->img[0], b->ss, c.rms_norm_eps, B},
+    BT_CUDA_CHECK(launch_gemm_digits(UnitW{e->head, V, unit_rows(V), D}, gin(b->img[0], b->ss, c.rms_norm_eps),
                                      GEpiLogits{b->logits, b->am_val, b->am_idx, V, nob}, err, nsm, s));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     batch_finish_kernel<<<(B + 7) / 8, 256, 0, s>>>(b->am_val, b->am_idx, nob, B, b->max_seq, b->pos, b->cur,
@@ -376,12 +482,68 @@ int check_batch(bt_batch* b) {
 
 extern "C" {
 
-int bt_batch_create(bt_engine* e, uint32_t n_seq, uint32_t max_seq, int kv_dtype, bt_batch** out) {
+}  // extern "C"
+
+namespace {
+
+constexpr uint32_t kNoPage = 0xFFFFFFFFu;
+
+// Paged KV: gives sequence s pages for its positions [0, n), taking pages from
+// the pool for the page-sized runs it does not hold yet and uploading those
+// table entries on stream st (ordered before the kernels that use them).
+// BT_ERR_OUT_OF_MEMORY, with nothing taken, when the pool has too few pages.
+int ensure_pages(bt_batch* b, uint32_t s, uint32_t n, cudaStream_t st) {
+    if (!b->paged || n == 0) return BT_OK;
+    const uint32_t need = (n + (1u << b->page_shift) - 1u) >> b->page_shift;
+    if (need > b->max_pages) return fail(BT_ERR_OUT_OF_RANGE, "KVCache pos out of bounds");
+    const uint32_t have = b->seq_pages[s];
+    if (need <= have) return BT_OK;
+    if (need - have > b->free_pages.size())
+        return fail(BT_ERR_OUT_OF_MEMORY, "paged KV: the page pool has too few free pages");
+    uint32_t* row = b->host_table.data() + (size_t)s * b->max_pages;
+    for (uint32_t j = have; j < need; ++j) {
+        row[j] = b->free_pages.back();
+        b->free_pages.pop_back();
+    }
+    b->seq_pages[s] = need;
+    // from pageable memory: staged before the call returns, so the host table may change afterwards
+    BT_CUDA_CHECK(cudaMemcpyAsync(b->table + (size_t)s * b->max_pages + have, row + have,
+                                  sizeof(uint32_t) * (need - have), cudaMemcpyHostToDevice, st));
+    return BT_OK;
+}
+
+// Paged KV: returns sequence s's pages to the pool and marks it idle (no work in
+// later steps).  The caller has synchronised the streams that used the pages.
+int drop_pages(bt_batch* b, uint32_t s, cudaStream_t st) {
+    uint32_t* row = b->host_table.data() + (size_t)s * b->max_pages;
+    for (uint32_t j = 0; j < b->seq_pages[s]; ++j) {
+        b->free_pages.push_back(row[j]);
+        row[j] = kNoPage;
+    }
+    b->seq_pages[s] = 0;
+    const uint32_t idle = 0xFFFFFFFFu;  // position "not started": the kernels skip the sequence
+    BT_CUDA_CHECK(cudaMemcpyAsync(b->table + (size_t)s * b->max_pages, row, sizeof(uint32_t) * b->max_pages,
+                                  cudaMemcpyHostToDevice, st));
+    BT_CUDA_CHECK(cudaMemcpyAsync(b->pos + s, &idle, sizeof(idle), cudaMemcpyHostToDevice, st));
+    BT_CUDA_CHECK(cudaStreamSynchronize(st));
+    b->host_pos[s] = b->max_seq;
+    return BT_OK;
+}
+
+// A batch with contiguous per-sequence caches (page_tokens 0) or with its KV in a
+// pool of n_pages pages of page_tokens positions.
+int batch_create(bt_engine* e, uint32_t n_seq, uint32_t max_seq, int kv_dtype, uint32_t page_tokens,
+                 uint32_t n_pages, bt_batch** out) {
     if (!e || !out) return fail(BT_ERR_INVALID_ARGUMENT, "bt_batch_create: null argument");
     *out = nullptr;
     if (n_seq == 0 || max_seq == 0) return fail(BT_ERR_INVALID_ARGUMENT, "bt_batch_create: n_seq and max_seq must be > 0");
     if (kv_dtype != BT_KV_FP32 && kv_dtype != BT_KV_FP16) return fail(BT_ERR_INVALID_ARGUMENT, "bt_batch_create: bad kv dtype");
     if (e->tp_world > 1) return fail(BT_ERR_INVALID_ARGUMENT, "bt_batch_create: not available under tensor parallelism");
+    if (page_tokens) {
+        if (page_tokens < 16 || page_tokens > 4096 || (page_tokens & (page_tokens - 1)))
+            return fail(BT_ERR_INVALID_ARGUMENT, "bt_batch_create_paged: page_tokens must be a power of two in [16, 4096]");
+        if (n_pages == 0) return fail(BT_ERR_INVALID_ARGUMENT, "bt_batch_create_paged: n_pages must be > 0");
+    }
     DeviceGuard guard(e->device);
     const auto& c = e->lc;
     auto b = new bt_batch();
@@ -398,14 +560,39 @@ int bt_batch_create(bt_engine* e, uint32_t n_seq, uint32_t max_seq, int kv_dtype
     const size_t esz = kv_dtype == BT_KV_FP16 ? 2 : 4;
     const uint32_t D = c.dim, F = c.hidden_dim, Q = qd(c), V = c.vocab_size, hd = c.head_dim;
     const uint32_t GQ = c.num_heads / c.num_kv_heads;
-    b->seq_stride = (size_t)c.num_layers * c.num_kv_heads * max_seq * hd;
-    const size_t n = b->seq_stride * n_seq;
+    size_t n = 0;  // cache elements (K, and again V)
+    b->map.hd = hd;
+    b->map.max_seq = max_seq;
+    if (page_tokens) {
+        b->paged = true;
+        while ((1u << b->page_shift) < page_tokens) ++b->page_shift;
+        b->n_pages = n_pages;
+        b->max_pages = (max_seq + page_tokens - 1) / page_tokens;
+        b->layer_stride = (size_t)c.num_kv_heads * page_tokens * hd;
+        b->map.page_stride = b->layer_stride * c.num_layers;
+        b->map.page_shift = b->page_shift;
+        b->map.max_pages = b->max_pages;
+        n = b->map.page_stride * n_pages;
+    } else {
+        b->seq_stride = (size_t)c.num_layers * c.num_kv_heads * max_seq * hd;
+        b->layer_stride = (size_t)c.num_kv_heads * max_seq * hd;
+        b->map.seq_stride = b->seq_stride;
+        n = b->seq_stride * n_seq;
+    }
     uint8_t *kb = nullptr, *vb = nullptr;
     int rc;
     if ((rc = dev_alloc(b->allocs, &kb, n * esz, "batch K cache"))) return cleanup(rc);
     if ((rc = dev_alloc(b->allocs, &vb, n * esz, "batch V cache"))) return cleanup(rc);
     b->k = kb;
     b->v = vb;
+    if (b->paged) {
+        if ((rc = dev_alloc(b->allocs, &b->table, (size_t)n_seq * b->max_pages, "page table"))) return cleanup(rc);
+        b->map.table = b->table;
+        b->host_table.assign((size_t)n_seq * b->max_pages, kNoPage);
+        b->seq_pages.assign(n_seq, 0);
+        b->free_pages.resize(n_pages);
+        for (uint32_t i = 0; i < n_pages; ++i) b->free_pages[i] = n_pages - 1 - i;  // page 0 is taken first
+    }
     if ((rc = dev_alloc(b->allocs, &b->rope, (size_t)max_seq * (hd / 2), "rope table"))) return cleanup(rc);
     if ((rc = dev_alloc(b->allocs, &b->pos, n_seq, "positions"))) return cleanup(rc);
     if ((rc = dev_alloc(b->allocs, &b->cur, n_seq, "current tokens"))) return cleanup(rc);
@@ -428,6 +615,9 @@ int bt_batch_create(bt_engine* e, uint32_t n_seq, uint32_t max_seq, int kv_dtype
     b->S = (max_seq + b->kps - 1) / b->kps;
     if ((rc = dev_alloc(b->allocs, &b->att_part, (size_t)n_seq * c.num_kv_heads * b->S * GQ * (hd + 2), "splits")))
         return cleanup(rc);
+    // split-K partials: a GEMM with fewer units than SMs is cut into up to about two units per SM
+    b->gpart_floats = gemm_split_floats(e->num_sms);
+    if ((rc = dev_alloc(b->allocs, &b->gpart, b->gpart_floats, "GEMM split partials"))) return cleanup(rc);
     const size_t nob = unit_rows(V) / 32;
     if ((rc = dev_alloc(b->allocs, &b->am_val, (size_t)n_seq * nob, "argmax partials"))) return cleanup(rc);
     if ((rc = dev_alloc(b->allocs, &b->am_idx, (size_t)n_seq * nob, "argmax partials"))) return cleanup(rc);
@@ -440,6 +630,9 @@ int bt_batch_create(bt_engine* e, uint32_t n_seq, uint32_t max_seq, int kv_dtype
     if (ce == cudaSuccess) ce = cudaMemsetAsync(b->cur, 0, sizeof(uint32_t) * n_seq, s);
     if (ce == cudaSuccess) ce = cudaMemsetAsync(b->n_fixed, 0, sizeof(uint32_t) * n_seq, s);
     if (ce == cudaSuccess) ce = cudaMemsetAsync(b->tok_hist, 0, sizeof(uint32_t) * n_seq * (max_seq + 1), s);
+    if (ce == cudaSuccess && b->paged)
+        ce = cudaMemcpyAsync(b->table, b->host_table.data(), sizeof(uint32_t) * b->host_table.size(),
+                             cudaMemcpyHostToDevice, s);
     std::vector<float2> tab((size_t)max_seq * (hd / 2));
     for (uint32_t i = 0; i < hd / 2; ++i) {
         const float freq = 1.0f / std::pow(e->theta, (float)(2 * i) / (float)hd);  // kernels/cpu_ref.hpp:40-43
@@ -454,6 +647,37 @@ int bt_batch_create(bt_engine* e, uint32_t n_seq, uint32_t max_seq, int kv_dtype
     if (ce != cudaSuccess) return cleanup(fail(BT_ERR_CUDA, cudaGetErrorString(ce)));
     b->host_pos.assign(n_seq, max_seq);
     *out = b;
+    return BT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bt_batch_create(bt_engine* e, uint32_t n_seq, uint32_t max_seq, int kv_dtype, bt_batch** out) {
+    return batch_create(e, n_seq, max_seq, kv_dtype, 0, 0, out);
+}
+
+int bt_batch_create_paged(bt_engine* e, uint32_t n_seq, uint32_t max_seq, uint32_t page_tokens, uint32_t n_pages,
+                          int kv_dtype, bt_batch** out) {
+    return batch_create(e, n_seq, max_seq, kv_dtype, page_tokens, n_pages, out);
+}
+
+int bt_batch_release(bt_batch* b, uint32_t s) {
+    int rc = check_batch(b);
+    if (rc != BT_OK) return rc;
+    if (s >= b->n_seq) return fail(BT_ERR_OUT_OF_RANGE, "bt_batch_release: sequence index out of range");
+    if (!b->paged) return fail(BT_ERR_INVALID_ARGUMENT, "bt_batch_release: the batch has no page pool");
+    DeviceGuard guard(b->e->device);
+    BT_CUDA_CHECK(cudaStreamSynchronize(b->e->stream));
+    return drop_pages(b, s, b->e->stream);
+}
+
+int bt_batch_pages(bt_batch* b, uint32_t* free_pages, uint32_t* total_pages) {
+    int rc = check_batch(b);
+    if (rc != BT_OK) return rc;
+    if (free_pages) *free_pages = b->paged ? (uint32_t)b->free_pages.size() : 0u;
+    if (total_pages) *total_pages = b->paged ? b->n_pages : 0u;
     return BT_OK;
 }
 
@@ -484,8 +708,19 @@ int bt_batch_prefill(bt_batch* b, uint32_t s, const uint32_t* prompt, uint32_t n
     if (rc != BT_OK) return rc;
     cudaStream_t st = e->stream;
     const size_t esz = b->dtype == BT_KV_FP16 ? 2 : 4;
-    const CacheRef cr{static_cast<uint8_t*>(b->k) + (size_t)s * b->seq_stride * esz,
-                      static_cast<uint8_t*>(b->v) + (size_t)s * b->seq_stride * esz, b->rope, b->max_seq, b->err};
+    CacheRef cr{static_cast<uint8_t*>(b->k), static_cast<uint8_t*>(b->v), b->rope, b->max_seq, b->err,
+                kv_map_flat(b->max_seq, e->lc.head_dim), b->layer_stride};
+    if (b->paged) {
+        // a new sequence in this slot: the previous one's pages go back to the pool first
+        BT_CUDA_CHECK(cudaStreamSynchronize(st));
+        if (b->seq_pages[s] && (rc = drop_pages(b, s, st)) != BT_OK) return rc;
+        if ((rc = ensure_pages(b, s, n_prompt, st)) != BT_OK) return rc;
+        cr.map = b->map;
+        cr.map.table = b->table + (size_t)s * b->max_pages;  // the sequence's row: index 0 in the map
+    } else {
+        cr.k = static_cast<uint8_t*>(b->k) + (size_t)s * b->seq_stride * esz;
+        cr.v = static_cast<uint8_t*>(b->v) + (size_t)s * b->seq_stride * esz;
+    }
     const uint32_t n_fill = n_prompt - 1;
     for (uint32_t done = 0; done < n_fill;) {
         const uint32_t T = std::min(n_fill - done, e->pf_cap);
@@ -514,11 +749,26 @@ int bt_batch_steps(bt_batch* b, uint32_t n, void* stream) {
     int rc = check_batch(b);
     if (rc != BT_OK) return rc;
     bt_engine* e = b->e;
-    for (uint32_t s = 0; s < b->n_seq; ++s)
+    for (uint32_t s = 0; s < b->n_seq; ++s) {
+        if (b->paged && b->seq_pages[s] == 0) continue;  // an idle slot of the page pool: no work
         if ((uint64_t)b->host_pos[s] + n > b->max_seq)
             return fail(BT_ERR_OUT_OF_RANGE, "bt_batch_steps: a sequence would pass max_seq (or was not prefilled)");
+    }
     DeviceGuard guard(e->device);
     cudaStream_t s = stream ? as_stream(stream) : e->stream;
+    if (b->paged) {
+        // pages for every position the n steps write (all or nothing: count them first)
+        size_t need = 0;
+        for (uint32_t q = 0; q < b->n_seq; ++q) {
+            if (b->seq_pages[q] == 0) continue;
+            const uint32_t want = (b->host_pos[q] + n + (1u << b->page_shift) - 1u) >> b->page_shift;
+            if (want > b->seq_pages[q]) need += want - b->seq_pages[q];
+        }
+        if (need > b->free_pages.size())
+            return fail(BT_ERR_OUT_OF_MEMORY, "paged KV: the page pool has too few free pages for these steps");
+        for (uint32_t q = 0; q < b->n_seq; ++q)
+            if (b->seq_pages[q] && (rc = ensure_pages(b, q, b->host_pos[q] + n, s)) != BT_OK) return rc;
+    }
     for (uint32_t i = 0; i < n; ++i) {
         if (!b->warmed) {
             // the first step runs eagerly: it sets every kernel's attributes outside capture
@@ -553,7 +803,8 @@ int bt_batch_steps(bt_batch* b, uint32_t n, void* stream) {
             BT_CUDA_CHECK(cudaGraphLaunch(b->graph, s));
         }
     }
-    for (uint32_t q = 0; q < b->n_seq; ++q) b->host_pos[q] += n;
+    for (uint32_t q = 0; q < b->n_seq; ++q)
+        if (!(b->paged && b->seq_pages[q] == 0)) b->host_pos[q] += n;
     return BT_OK;
 }
 

@@ -182,6 +182,40 @@ template <> struct KVConv<__half> {
     __device__ static __half from_f(float v) { return __float2half_rn(v); }
 };
 
+// Where the K (or V) row of (sequence, KV head, position) of one layer lives, in
+// elements from that layer's base pointer.
+//   contiguous (table null): every sequence owns [L][KVH][max_seq][hd], so
+//     row = seq * seq_stride + (h * max_seq + pos) * hd, the layer's offset in the base;
+//   paged: a pool of pages of 2^page_shift positions, a page holding every layer's
+//     [KVH][2^page_shift][hd] rows; table[seq * max_pages + pos >> page_shift] names
+//     the page of a position, so row = page * page_stride + (h 2^page_shift +
+//     pos mod 2^page_shift) * hd, the layer's offset inside a page in the base.
+// Callers bound pos by max_seq (positions a sequence may hold) before asking.
+struct KVMap {
+    const uint32_t* table = nullptr;
+    size_t seq_stride = 0;
+    size_t page_stride = 0;
+    uint32_t max_seq = 0;
+    uint32_t max_pages = 0;
+    uint32_t page_shift = 0;
+    uint32_t hd = 0;
+    __host__ __device__ __forceinline__ bool paged() const { return table != nullptr; }
+    __device__ __forceinline__ size_t row(uint32_t seq, uint32_t h, uint32_t pos) const {
+        if (!table) return (size_t)seq * seq_stride + ((size_t)h * max_seq + pos) * hd;
+        const uint32_t pg = __ldg(table + (size_t)seq * max_pages + (pos >> page_shift));
+        const uint32_t in_page = pos & ((1u << page_shift) - 1u);
+        return (size_t)pg * page_stride + ((size_t)h * (1u << page_shift) + in_page) * hd;
+    }
+};
+
+// The contiguous map of one sequence's cache [KVH][max_seq][hd] (sequence index 0).
+inline KVMap kv_map_flat(uint32_t max_seq, uint32_t hd) {
+    KVMap m;
+    m.max_seq = max_seq;
+    m.hd = hd;
+    return m;
+}
+
 // Cache element loaded through L2 (rows may have been written by another SM in the same kernel).
 __device__ __forceinline__ float ldcg_kv(const float* p) { return __ldcg(p); }
 __device__ __forceinline__ __half ldcg_kv(const __half* p) {

@@ -107,7 +107,9 @@ int plan_step(bt_engine* e) {
     if (qd(c) > kmax) kmax = qd(c);
     const size_t img_bytes = mma_digit_bytes(kmax);  // digits + block factors
     size_t scratch = img_bytes;
-    const size_t attn = (size_t)kDigitWarps * GQ * (hd + 2) * 4;
+    // attention: the warps' partials [9][GQ][hd + 2], then (grouped heads) q's tensor-core
+    // fragments, 16 bytes per lane and k-step, 16-byte aligned
+    const size_t attn = ((size_t)kDigitWarps * GQ * (hd + 2) * 4 + 15) / 16 * 16 + (size_t)32 * (hd / 8) * 16;
     if (attn > scratch) scratch = attn;
     scratch = (scratch + 127) / 128 * 128;
     const size_t budget = 220 * 1024;
@@ -767,7 +769,7 @@ int bt_kv_create(bt_engine* e, uint32_t max_seq, int dtype, bt_kv** out) {
     if ((rc = dev_alloc(kv->allocs, &kv->att_ticket, (size_t)c.num_layers * c.num_kv_heads, "attention tickets")))
         return cleanup(rc);
     // persistent step kernel: one attention item per (KV head, split), about one per SM, at most
-    // kAttnMaxSplits splits per head (split 0's CTA holds them all in registers when it merges)
+    // kAttnMaxSplits splits per head (split 0's CTA merges the others' partials in split order)
     kv->step_S = e->num_sms / c.num_kv_heads;
     if (kv->step_S < 1) kv->step_S = 1;
     if (kv->step_S > kAttnMaxSplits) kv->step_S = kAttnMaxSplits;
@@ -944,7 +946,7 @@ int bt_engine_set_trace(bt_engine* e, int enable) {
     if (enable && !e->trace) {
         size_t n = (size_t)(5 * e->lc.num_layers + 1) * e->num_sms * kTraceSlots;
 #ifdef BT_STAGE_TRACE
-        n += (size_t)e->num_sms * kStageTraceMax * 4;
+        n += (size_t)e->num_sms * kStageTraceMax * kStageSlots;
 #endif
         BT_TRY_ALLOC(e->allocs, &e->trace, n, "step trace");
         BT_CUDA_CHECK(cudaMemset(e->trace, 0, n * sizeof(uint64_t)));
@@ -966,7 +968,7 @@ int bt_engine_read_trace(bt_engine* e, uint64_t* out, uint64_t n_words) {
     if (!e->trace) return fail(BT_ERR_INVALID_ARGUMENT, "trace is off (bt_engine_set_trace)");
     uint64_t n = (uint64_t)(5 * e->lc.num_layers + 1) * e->num_sms * kTraceSlots;
 #ifdef BT_STAGE_TRACE
-    n += (uint64_t)e->num_sms * kStageTraceMax * 4;  // a stage-trace build: the stage timeline follows
+    n += (uint64_t)e->num_sms * kStageTraceMax * kStageSlots;  // a stage-trace build: the stage timeline follows
 #endif
     if (n_words != n) return fail(BT_ERR_INVALID_ARGUMENT, "read_trace: n_words does not match the trace size");
     DeviceGuard guard(e->device);

@@ -87,6 +87,8 @@ struct bt_engine {
     uint8_t* pf_img[2] = {nullptr, nullptr};  // token images (K = D or DQ; K = F or DQ)
     uint32_t* pf_tok = nullptr; // [cap] token ids
     uint32_t* pf_pos = nullptr; // [cap] positions
+    float* pf_part = nullptr;   // split-K partial sums of chunk GEMMs with fewer units than SMs
+    size_t pf_part_floats = 0;
 };
 
 struct bt_kv {
@@ -117,11 +119,13 @@ namespace bt {
 // One sequence's KV cache as prefill sees it: K and V [L][KVH][max_seq][hd] (fp32 or
 // fp16 by the engine call), the RoPE table, and the flag bounded waits set.
 struct CacheRef {
-    void* k;
+    void* k;              // layer 0's K base (row addresses from map)
     void* v;
     const float2* rope;
-    uint32_t max_seq;
+    uint32_t max_seq;     // positions the sequence may hold
     uint32_t* err;
+    KVMap map;            // rows of the sequence (index 0 of the map)
+    size_t layer_stride;  // elements between two layers' bases
 };
 
 // Prompt prefill building blocks (bt_prefill.cu).

@@ -81,14 +81,26 @@ struct GemmTok {
     const uint32_t* seq;     // sequence (KV cache) of token t; null: all tokens in cache 0
 };
 
-// RMSNorm factor of token t from its per-block sums of squares ss[t][0..NB):
-// 1/sqrt(sum/K + eps) (kernels/cpu_ref.hpp:11-28), summed by the warp.
-__device__ __forceinline__ float token_inv(const float* ss, uint32_t NB, uint32_t K, float eps, uint32_t t,
-                                           uint32_t lane) {
-    float s = 0.0f;
-    for (uint32_t b = lane; b < NB; b += 32) s += __ldcg(ss + (size_t)t * NB + b);
-    s = warp_sum(s);
-    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)K), eps)));
+// RMSNorm factors of tokens tok0 .. tok0 + nvalid - 1, multiplied into v[i]:
+// token_inv for 16 tokens with every token's loads in flight together (the same
+// sums in the same order).
+__device__ __forceinline__ void scale_by_token_inv(float (&v)[16], const float* ss, uint32_t NB, uint32_t K, float eps,
+                                                   uint32_t tok0, uint32_t nvalid, uint32_t lane) {
+    float s[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) s[i] = 0.0f;
+    for (uint32_t b = lane; b < NB; b += 32) {
+        float t[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) t[i] = (uint32_t)i < nvalid ? __ldcg(ss + (size_t)(tok0 + i) * NB + b) : 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) s[i] += t[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float tot = warp_sum(s[i]);
+        if ((uint32_t)i < nvalid) v[i] *= __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), eps)));
+    }
 }
 
 // ---------------------------------------------------------------- epilogues
@@ -127,12 +139,16 @@ struct GEpiResidual {
         const uint32_t NB = D / 32;
         if (ob >= NB) return;  // padding rows of the last row tile (warp-uniform: D is a multiple of 32)
         const float w = w_next[r];
+        // the 16 tokens' x first, all loads in flight (the stores below would order them otherwise)
+        float xo[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) xo[i] = (uint32_t)i < nvalid ? __ldcg(x + (size_t)(tok0 + i) * D + r) : 0.0f;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
             if ((uint32_t)i >= nvalid) break;
             const uint32_t t = tok0 + i;
             float* xp = x + (size_t)t * D + r;
-            const float xn = __fadd_rn(__ldcg(xp), v[i]);
+            const float xn = __fadd_rn(xo[i], v[i]);
             *xp = xn;
             if (tap) tap[(size_t)t * D + r] = xn;
             token_digits(img_next, NB, t, ob, xn * w, lane);
@@ -185,44 +201,51 @@ struct GEpiSwiGLU {
 template <typename KVT>
 struct GEpiQKV {
     float* q;              // [T][DQ]
-    KVT* kc;               // [seq][L][KVH][max_seq][hd] (this layer's offset applied)
+    KVT* kc;               // this layer's K cache base (row addresses from map)
     KVT* vc;
-    size_t seq_stride;     // elements between sequences
+    KVMap map;             // contiguous or paged rows; map.max_seq bounds the positions
     const float2* rope;    // [max_seq][hd/2]
     GemmTok tk;
-    uint32_t DQ, KVD, hd, max_seq;
+    uint32_t DQ, KVD, hd;
     template <class Bar>
     __device__ void rows(uint32_t r, uint32_t, uint32_t tok0, uint32_t nvalid, const float (&v)[16], uint32_t lane,
                          uint32_t, float*, Bar) const {
         const uint32_t half = hd >> 1;
+        const bool isq = r < DQ, isk = !isq && r < DQ + KVD, isv = r >= DQ + KVD && r < DQ + 2 * KVD;
+        const uint32_t local = isq ? r : isk ? r - DQ : r - DQ - KVD;
+        const uint32_t h = local / hd, j = (local % hd) >> 1;
+        // every token's position, RoPE factors and cache row first, all loads in flight (the
+        // stores below would order them otherwise)
+        uint32_t pos[16];
+        float2 cs[16];
+        size_t ro[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            pos[i] = (uint32_t)i < nvalid ? tk.pos[tok0 + i] : 0xFFFFFFFFu;
+            const bool live = pos[i] < map.max_seq;
+            cs[i] = (live && (isq || isk)) ? rope[(size_t)pos[i] * half + j] : make_float2(1.0f, 0.0f);
+            const uint32_t seq = (live && tk.seq) ? tk.seq[tok0 + i] : 0u;
+            ro[i] = (live && (isk || isv)) ? map.row(seq, h, pos[i]) : 0;
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
             const float partner = __shfl_xor_sync(0xffffffffu, v[i], 1);
-            if ((uint32_t)i >= nvalid) continue;
+            if (pos[i] >= map.max_seq) continue;  // also tokens >= nvalid
             const uint32_t t = tok0 + i;
-            const uint32_t pos = tk.pos[t];
-            if (pos >= max_seq) continue;
-            const size_t so = tk.seq ? (size_t)tk.seq[t] * seq_stride : 0;
-            if (r < DQ + KVD) {
-                const bool isq = r < DQ;
-                const uint32_t local = isq ? r : r - DQ;
-                const uint32_t h = local / hd, j = (local % hd) >> 1;
-                const float2 cs = rope[(size_t)pos * half + j];
+            if (isq || isk) {
                 float o;
                 uint32_t d;
                 if ((lane & 1) == 0) {  // first of the pair: a cos - b sin
-                    o = __fsub_rn(__fmul_rn(v[i], cs.x), __fmul_rn(partner, cs.y));
+                    o = __fsub_rn(__fmul_rn(v[i], cs[i].x), __fmul_rn(partner, cs[i].y));
                     d = j;
                 } else {                // second: a sin + b cos
-                    o = __fadd_rn(__fmul_rn(partner, cs.y), __fmul_rn(v[i], cs.x));
+                    o = __fadd_rn(__fmul_rn(partner, cs[i].y), __fmul_rn(v[i], cs[i].x));
                     d = j + half;
                 }
                 if (isq) q[(size_t)t * DQ + h * hd + d] = o;
-                else kc[so + ((size_t)h * max_seq + pos) * hd + d] = KVConv<KVT>::from_f(o);
-            } else if (r < DQ + 2 * KVD) {
-                const uint32_t local = r - DQ - KVD;
-                const uint32_t h = local / hd, d = local % hd;
-                vc[so + ((size_t)h * max_seq + pos) * hd + d] = KVConv<KVT>::from_f(v[i]);
+                else kc[ro[i] + d] = KVConv<KVT>::from_f(o);
+            } else if (isv) {
+                vc[ro[i] + local % hd] = KVConv<KVT>::from_f(v[i]);
             }
         }
     }
@@ -235,7 +258,18 @@ struct GemmIn {
     const float* ss;       // per-block sums of squares [T][NB] of the RMSNorm input (null: no norm)
     float eps;
     uint32_t T;
+    // split-K workspace: with more splits than one the units write their partial sums
+    // [KS][T][Mp] here and gemm_reduce_kernel sums them and runs the epilogue
+    float* part = nullptr;
+    size_t part_floats = 0;
+    uint32_t KS = 1;       // set by launch_gemm_digits
 };
+
+// Blocks [b0, b1) of K-split ks of KS.
+__device__ __forceinline__ void split_blocks(uint32_t NB, uint32_t ks, uint32_t KS, uint32_t& b0, uint32_t& b1) {
+    b0 = (uint32_t)(((uint64_t)NB * ks) / KS);
+    b1 = (uint32_t)(((uint64_t)NB * (ks + 1)) / KS);
+}
 
 template <class Epi>
 __global__ void __launch_bounds__(kGThreads, 1) gemm_digits_kernel(UnitW W, GemmIn in, Epi epi, uint32_t NS,
@@ -246,9 +280,9 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_digits_kernel(UnitW W, Gemm
     __shared__ uint32_t s_tmem;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t NB = W.K / kTileK, NTG = token_groups(in.T);
-    const uint32_t units = (W.Mp / kTileRows) * NTG;
-    const uint32_t nst = (NB + kGStageBlocks - 1) / kGStageBlocks;  // stages per unit
+    const uint32_t NB = W.K / kTileK, NTG = token_groups(in.T), KS = in.KS;
+    // a unit: (row tile g, token group tg, K-split ks), consecutive units sharing a row tile
+    const uint32_t units = (W.Mp / kTileRows) * NTG * KS;
     uint8_t* ring = smem;
     float* exch = reinterpret_cast<float*>(smem + (size_t)kGMaxStages * kGStageBytes);
 
@@ -278,10 +312,12 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_digits_kernel(UnitW W, Gemm
             uint32_t s = 0, ph = 0, issued = 0;
             bool ok = true;
             for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
-                const uint32_t g = u / NTG, tg = u % NTG;
-                for (uint32_t st = 0; st < nst; ++st) {
+                const uint32_t ks = u % KS, g = (u / KS) / NTG, tg = (u / KS) % NTG;
+                uint32_t bs, be;
+                split_blocks(NB, ks, KS, bs, be);
+                for (uint32_t b0 = bs; b0 < be; b0 += kGStageBlocks) {
                     if (issued >= NS && !(ok = mbar_wait(&empty[s], ph ^ 1, err))) break;
-                    const uint32_t b0 = st * kGStageBlocks, n = min(kGStageBlocks, NB - b0);
+                    const uint32_t n = min(kGStageBlocks, be - b0);
                     mbar_expect_tx(&full[s], n * (kTileBytes + kGDTile));
                     uint8_t* dst = ring + (size_t)s * kGStageBytes;
                     bulk_g2s(dst, W.units + ((size_t)g * NB + b0) * kTileBytes, n * kTileBytes, &full[s]);
@@ -303,8 +339,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_digits_kernel(UnitW W, Gemm
             bool ok = true;
             uint32_t s = 0, ph = 0, j = 0;
             for (uint32_t u = blockIdx.x; u < units; u += gridDim.x) {
-                for (uint32_t st = 0; st < nst; ++st) {
-                    const uint32_t b0 = st * kGStageBlocks, n = min(kGStageBlocks, NB - b0);
+                uint32_t bs, be;
+                split_blocks(NB, u % KS, KS, bs, be);
+                for (uint32_t b0 = bs; b0 < be; b0 += kGStageBlocks) {
+                    const uint32_t n = min(kGStageBlocks, be - b0);
                     if (ok) ok = mbar_wait(&full[s], ph, err);
                     tcgen05_fence_after();
                     const uint8_t* stage = ring + (size_t)s * kGStageBytes;
@@ -341,12 +379,14 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_digits_kernel(UnitW W, Gemm
     bool ok = true;
     uint32_t s = 0, ph = 0, j = 0;
     for (uint32_t u = blockIdx.x; u < units; u += gridDim.x) {
-        const uint32_t g = u / NTG, tg = u % NTG;
+        const uint32_t ks = u % KS, g = (u / KS) / NTG, tg = (u / KS) % NTG;
+        uint32_t bs, be;
+        split_blocks(NB, ks, KS, bs, be);
         float acc[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
-        for (uint32_t st = 0; st < nst; ++st) {
-            const uint32_t b0 = st * kGStageBlocks, n = min(kGStageBlocks, NB - b0);
+        for (uint32_t b0 = bs; b0 < be; b0 += kGStageBlocks) {
+            const uint32_t n = min(kGStageBlocks, be - b0);
             const uint8_t* stage = ring + (size_t)s * kGStageBytes;
             // the scales and block factors this warp reads were written by the stage's bulk copies
             if (ok) ok = mbar_wait(&full[s], ph, err);
@@ -383,17 +423,15 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_digits_kernel(UnitW W, Gemm
         // ---------------- epilogue of the unit
         const uint32_t tok0 = tg * kGTok + 16 * h;
         const uint32_t nvalid = tok0 < in.T ? min(16u, in.T - tok0) : 0u;
-        if (in.ss) {
-            const uint32_t NBin = NB;
-#pragma unroll 1
-            for (uint32_t i = 0; i < 16; ++i) {
-                if (i >= nvalid) break;
-                const float inv = token_inv(in.ss, NBin, W.K, in.eps, tok0 + i, lane);
+        if (KS > 1) {
+            // one K-split's partial sums; gemm_reduce_kernel adds the splits and runs the epilogue
+            const uint32_t r = g * kTileRows + row;
 #pragma unroll
-                for (int k = 0; k < 16; ++k)
-                    if ((uint32_t)k == i) acc[k] *= inv;
-            }
+            for (int i = 0; i < 16; ++i)
+                if ((uint32_t)i < nvalid) in.part[((size_t)ks * in.T + tok0 + i) * W.Mp + r] = acc[i];
+            continue;
         }
+        if (in.ss) scale_by_token_inv(acc, in.ss, NB, W.K, in.eps, tok0, nvalid, lane);
         const uint32_t r = g * kTileRows + row;
         epi.rows(r, r >> 5, tok0, nvalid, acc, lane, q, ex, bar);
     }
@@ -425,15 +463,62 @@ static __global__ void __launch_bounds__(256) token_image_kernel(const float* __
     }
 }
 
+// The K-splits of a GEMM added in split order, the RMSNorm factor applied, and
+// the epilogue run as the GEMM's readers run it: one CTA of 4 warps per (row
+// tile, token group, token half), warp q holding rows 32 q .. 32 q + 31.
+template <class Epi>
+__global__ void __launch_bounds__(128) gemm_reduce_kernel(UnitW W, GemmIn in, Epi epi) {
+    __shared__ float ex[16 * 64];
+    const uint32_t q = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t NTG = token_groups(in.T), NB = W.K / kTileK;
+    const uint32_t h = blockIdx.x & 1, tg = (blockIdx.x >> 1) % NTG, g = (blockIdx.x >> 1) / NTG;
+    const uint32_t r = g * kTileRows + 32 * q + lane;
+    const uint32_t tok0 = tg * kGTok + 16 * h;
+    const uint32_t nvalid = tok0 < in.T ? min(16u, in.T - tok0) : 0u;
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+    // split by split, the 16 tokens' loads of a split in flight together
+    for (uint32_t ks = 0; ks < in.KS; ++ks) {
+        const float* pk = in.part + ((size_t)ks * in.T + tok0) * W.Mp + r;
+        float t[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) t[i] = (uint32_t)i < nvalid ? __ldcg(pk + (size_t)i * W.Mp) : 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] += t[i];
+    }
+    if (in.ss) scale_by_token_inv(v, in.ss, NB, W.K, in.eps, tok0, nvalid, lane);
+    auto bar = []() { __syncthreads(); };
+    epi.rows(r, r >> 5, tok0, nvalid, v, lane, q, ex, bar);
+}
+
 // ---------------------------------------------------------------- host side
 
 inline uint32_t gemm_stages() { return (uint32_t)kGMaxStages; }
 
+// K-splits of a GEMM: enough units to give every SM one (at least 8 blocks per
+// split), within the workspace; 1 when there is no workspace.
+inline uint32_t gemm_splits(uint32_t Mp, uint32_t K, uint32_t T, uint32_t nsm, size_t part_floats) {
+    const uint32_t units = (Mp / kTileRows) * token_groups(T), NB = K / kTileK;
+    if (units == 0 || units >= nsm || part_floats == 0) return 1;
+    uint32_t ks = (nsm + units - 1) / units;
+    ks = ks < NB / 8 ? ks : NB / 8;
+    while (ks > 1 && (size_t)ks * T * Mp > part_floats) --ks;
+    return ks < 1 ? 1 : ks;
+}
+
+// Size of a split-K workspace that lets every GEMM reach about one unit per SM:
+// KS splits of U < nsm units need KS * T * Mp floats with KS * U <= ~2 nsm, and a
+// unit covers at most 128 rows x 32 tokens.
+inline size_t gemm_split_floats(uint32_t nsm) { return (size_t)2 * nsm * kTileRows * kGTok; }
+
 template <class Epi>
-cudaError_t launch_gemm_digits(const UnitW& W, const GemmIn& in, const Epi& epi, uint32_t* err, uint32_t nsm,
+cudaError_t launch_gemm_digits(const UnitW& W, const GemmIn& in_, const Epi& epi, uint32_t* err, uint32_t nsm,
                                cudaStream_t s) {
     if (W.K % kTileK || W.Mp % kTileRows || W.K == 0 || W.Mp == 0) return cudaErrorInvalidValue;
-    const uint32_t units = (W.Mp / kTileRows) * token_groups(in.T);
+    GemmIn in = in_;
+    in.KS = gemm_splits(W.Mp, W.K, in.T, nsm, in.part ? in.part_floats : 0);
+    const uint32_t units = (W.Mp / kTileRows) * token_groups(in.T) * in.KS;
     if (units == 0) return cudaSuccess;
     auto kern = gemm_digits_kernel<Epi>;
     static bool attr_set[64] = {};
@@ -446,7 +531,11 @@ cudaError_t launch_gemm_digits(const UnitW& W, const GemmIn& in, const Epi& epi,
         attr_set[dev] = true;
     }
     const uint32_t grid = units < nsm ? units : nsm;
-    return launch_pdl(kern, dim3(grid), dim3(kGThreads), (size_t)kGSmem, s, false, W, in, epi, gemm_stages(), err);
+    cudaError_t ce = launch_pdl(kern, dim3(grid), dim3(kGThreads), (size_t)kGSmem, s, false, W, in, epi,
+                                gemm_stages(), err);
+    if (ce != cudaSuccess || in.KS == 1) return ce;
+    const uint32_t reduce_ctas = (W.Mp / kTileRows) * token_groups(in.T) * 2;
+    return launch_pdl(gemm_reduce_kernel<Epi>, dim3(reduce_ctas), dim3(128), 0, s, false, W, in, epi);
 }
 
 }  // namespace bt

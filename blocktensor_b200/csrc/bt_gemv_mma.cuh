@@ -523,6 +523,7 @@ __device__ __forceinline__ void acc_stages(uint32_t u0, uint32_t u1, uint32_t NB
             sl[k] = s;
             nt[k] = 0;
             if (k < m) {
+                hook(j + k, 5);
                 if (ok) ok = mbar_wait(&mma_done[s], ph, err);
                 hook(j + k, 2);
                 tcgen05_fence_after();

@@ -53,11 +53,12 @@ int gemv_check_timeout(uint32_t* flag, uint32_t* tickets, size_t ticket_bytes, c
 // Sets the no-alloc GEMV's bounded-wait flag on `device` (host-side fault injection for tests).
 int noalloc_inject_timeout(int device);
 
-// The multi-token tensor-core GEMM (bt_prefill.cu): token image of X [T][K] into img
-// (gemm_units_scratch bytes), then Y [T][M] = X W^T.
+// The multi-token tensor-core GEMM (bt_prefill.cu): token image of X [T][K] into the
+// workspace ws (gemm_units_scratch bytes: the image, then split-K partial sums), then
+// Y [T][M] = X W^T.
 cudaError_t gemm_units_launch(const void* units, const float* X, float* Y, uint32_t M, uint32_t K, uint32_t T,
-                              uint8_t* img, uint32_t* err, uint32_t nsm, cudaStream_t s);
-size_t gemm_units_scratch(uint32_t K, uint32_t T);
+                              uint8_t* ws, uint32_t* err, uint32_t nsm, cudaStream_t s);
+size_t gemm_units_scratch(uint32_t K, uint32_t T, uint32_t nsm);
 
 // Same formula as the CPU oracle (oracle/bt_oracle.c bto_normal_k).
 float normal_k(float sigma);

@@ -45,7 +45,7 @@ template <int NVM, typename KVT>
 __global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restrict__ q, const KVT* __restrict__ kc,
                                                            const KVT* __restrict__ vc, float* __restrict__ out,
                                                            uint32_t T, uint32_t pos0, uint32_t H, uint32_t GQ,
-                                                           uint32_t hd, uint32_t max_seq, float scale) {
+                                                           uint32_t hd, KVMap map, float scale) {
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t t = blockIdx.y * 8 + (threadIdx.x >> 5);
     if (t >= T) return;
@@ -53,8 +53,6 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restri
     const uint32_t P = pos0 + t;
     const size_t DQ = (size_t)H * hd;
     const float* qp = q + (size_t)t * DQ + (size_t)h * hd;
-    const KVT* kb = kc + (size_t)kvh * max_seq * hd;
-    const KVT* vb = vc + (size_t)kvh * max_seq * hd;
     float qv[NVM], o[NVM];
 #pragma unroll
     for (int i = 0; i < NVM; ++i) {
@@ -69,12 +67,13 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restri
 #pragma unroll
         for (int j = 0; j < B; ++j) {
             const uint32_t key = base + j;
+            const size_t ro = key <= P ? map.row(0, kvh, key) : 0;
 #pragma unroll
             for (int i = 0; i < NVM; ++i) {
                 const uint32_t d = lane + 32 * i;
                 const bool ok = key <= P && d < hd;
-                kr[j][i] = ok ? KVConv<KVT>::to_f(kb[(size_t)key * hd + d]) : 0.0f;
-                vr[j][i] = ok ? KVConv<KVT>::to_f(vb[(size_t)key * hd + d]) : 0.0f;
+                kr[j][i] = ok ? KVConv<KVT>::to_f(kc[ro + d]) : 0.0f;
+                vr[j][i] = ok ? KVConv<KVT>::to_f(vc[ro + d]) : 0.0f;
             }
         }
         float sc[B];
@@ -117,14 +116,14 @@ __global__ void positions_kernel(uint32_t* pos, uint32_t T, uint32_t pos0) {
 
 template <typename KVT>
 cudaError_t launch_prefill_attn(const float* q, const KVT* kc, const KVT* vc, float* out, uint32_t T, uint32_t pos0,
-                                uint32_t H, uint32_t GQ, uint32_t hd, uint32_t max_seq, float scale, cudaStream_t s) {
+                                uint32_t H, uint32_t GQ, uint32_t hd, const KVMap& map, float scale, cudaStream_t s) {
     const dim3 grid(H, (T + 7) / 8);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     const uint32_t nv = (hd + 31) / 32;
-    if (nv <= 1) prefill_attn_kernel<1, KVT><<<grid, 256, 0, s>>>(q, kc, vc, out, T, pos0, H, GQ, hd, max_seq, scale);
-    else if (nv == 2) prefill_attn_kernel<2, KVT><<<grid, 256, 0, s>>>(q, kc, vc, out, T, pos0, H, GQ, hd, max_seq, scale);
-    else if (nv <= 4) prefill_attn_kernel<4, KVT><<<grid, 256, 0, s>>>(q, kc, vc, out, T, pos0, H, GQ, hd, max_seq, scale);
-    else prefill_attn_kernel<8, KVT><<<grid, 256, 0, s>>>(q, kc, vc, out, T, pos0, H, GQ, hd, max_seq, scale);
+    if (nv <= 1) prefill_attn_kernel<1, KVT><<<grid, 256, 0, s>>>(q, kc, vc, out, T, pos0, H, GQ, hd, map, scale);
+    else if (nv == 2) prefill_attn_kernel<2, KVT><<<grid, 256, 0, s>>>(q, kc, vc, out, T, pos0, H, GQ, hd, map, scale);
+    else if (nv <= 4) prefill_attn_kernel<4, KVT><<<grid, 256, 0, s>>>(q, kc, vc, out, T, pos0, H, GQ, hd, map, scale);
+    else prefill_attn_kernel<8, KVT><<<grid, 256, 0, s>>>(q, kc, vc, out, T, pos0, H, GQ, hd, map, scale);
     return cudaGetLastError();
 }
 
@@ -152,6 +151,8 @@ int ensure_prefill_buffers(bt_engine* e) {
     BT_TRY_ALLOC(A, &e->pf_img[1], token_image_bytes((uint32_t)cap, k1), "prefill token image");
     BT_TRY_ALLOC(A, &e->pf_tok, cap, "prefill tokens");
     BT_TRY_ALLOC(A, &e->pf_pos, cap, "prefill positions");
+    e->pf_part_floats = gemm_split_floats(e->num_sms);
+    BT_TRY_ALLOC(A, &e->pf_part, e->pf_part_floats, "prefill GEMM split partials");
     e->pf_cap = (uint32_t)cap;
     return BT_OK;
 }
@@ -163,39 +164,45 @@ int prefill_chunk_t(bt_engine* e, const CacheRef& kv, uint32_t T, uint32_t pos0,
     const uint32_t QKV = Q + 2 * KV, L = c.num_layers, nsm = e->num_sms;
     uint32_t* err = kv.err;
     const float scale = 1.0f / std::sqrt((float)hd);
+    // GEMM inputs with the split-K workspace (used by short chunks: fewer units than SMs)
+    auto gin = [&](const uint8_t* img, const float* ss, float eps) {
+        GemmIn g{img, ss, eps, T};
+        g.part = e->pf_part;
+        g.part_floats = e->pf_part_floats;
+        return g;
+    };
     positions_kernel<<<(T + 255) / 256, 256, 0, s>>>(e->pf_pos, T, pos0);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     BT_CUDA_CHECK(cudaGetLastError());
     // layer 0 input: the embedding rows (also the residual stream) times attn_norm
     BT_CUDA_CHECK(launch_token_image(e->embed, e->pf_tok, e->layers[0].attn_norm, T, D, e->pf_img[0], e->pf_ss,
                                      e->pf_x, s));
-    const size_t kv_layer = (size_t)c.num_kv_heads * kv.max_seq * hd;
     for (uint32_t l = 0; l < L; ++l) {
         const LayerDev& Ld = e->layers[l];
-        KVT* kl = static_cast<KVT*>(kv.k) + l * kv_layer;
-        KVT* vl = static_cast<KVT*>(kv.v) + l * kv_layer;
+        KVT* kl = static_cast<KVT*>(kv.k) + l * kv.layer_stride;
+        KVT* vl = static_cast<KVT*>(kv.v) + l * kv.layer_stride;
         // qkv + RoPE + K/V append
         {
-            GEpiQKV<KVT> epi{e->pf_q, kl, vl, 0, kv.rope, GemmTok{T, e->pf_pos, nullptr}, Q, KV, hd, kv.max_seq};
+            GEpiQKV<KVT> epi{e->pf_q, kl, vl, kv.map, kv.rope, GemmTok{T, e->pf_pos, nullptr}, Q, KV, hd};
             BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.qkv, QKV, unit_rows(QKV), D},
-                                             GemmIn{e->pf_img[0], e->pf_ss, c.rms_norm_eps, T}, epi, err, nsm, s));
+                                             gin(e->pf_img[0], e->pf_ss, c.rms_norm_eps), epi, err, nsm, s));
         }
         // causal attention over the cache, then the o-proj input's token image
         BT_CUDA_CHECK(launch_prefill_attn<KVT>(e->pf_q, kl, vl, e->pf_attn, T, pos0, c.num_heads,
-                                               c.num_heads / c.num_kv_heads, hd, kv.max_seq, scale, s));
+                                               c.num_heads / c.num_kv_heads, hd, kv.map, scale, s));
         BT_CUDA_CHECK(launch_token_image(e->pf_attn, nullptr, nullptr, T, Q, e->pf_img[1], nullptr, nullptr, s));
         // o-proj + residual; token image of x * ffn_norm
-        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.o, D, unit_rows(D), Q}, GemmIn{e->pf_img[1], nullptr, 0.0f, T},
+        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.o, D, unit_rows(D), Q}, gin(e->pf_img[1], nullptr, 0.0f),
                                          GEpiResidual{e->pf_x, Ld.ffn_norm, e->pf_img[0], e->pf_ss, nullptr, D}, err,
                                          nsm, s));
         // gate/up + SwiGLU; token image of act
         BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.gu, 2 * F, unit_rows(2 * F), D},
-                                         GemmIn{e->pf_img[0], e->pf_ss, c.rms_norm_eps, T},
+                                         gin(e->pf_img[0], e->pf_ss, c.rms_norm_eps),
                                          GEpiSwiGLU{e->pf_act, e->pf_img[1], F}, err, nsm, s));
         // down + residual; token image of x * the next layer's attn_norm (the last layer's output
         // is not used: the decode step processes the final prompt token)
         const float* wn = l + 1 < L ? e->layers[l + 1].attn_norm : e->out_norm;
-        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.d, D, unit_rows(D), F}, GemmIn{e->pf_img[1], nullptr, 0.0f, T},
+        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.d, D, unit_rows(D), F}, gin(e->pf_img[1], nullptr, 0.0f),
                                          GEpiResidual{e->pf_x, wn, e->pf_img[0], e->pf_ss, nullptr, D}, err, nsm,
                                          s));
     }
@@ -205,15 +212,23 @@ int prefill_chunk_t(bt_engine* e, const CacheRef& kv, uint32_t T, uint32_t pos0,
 template int prefill_chunk_t<float>(bt_engine*, const CacheRef&, uint32_t, uint32_t, cudaStream_t);
 template int prefill_chunk_t<__half>(bt_engine*, const CacheRef&, uint32_t, uint32_t, cudaStream_t);
 
+// Workspace of gemm_units_launch: the token image, then the split-K partials.
+static size_t image_part_offset(uint32_t K, uint32_t T) { return (token_image_bytes(T, K) + 255) / 256 * 256; }
+
 cudaError_t gemm_units_launch(const void* units, const float* X, float* Y, uint32_t M, uint32_t K, uint32_t T,
-                              uint8_t* img, uint32_t* err, uint32_t nsm, cudaStream_t s) {
-    cudaError_t ce = launch_token_image(X, nullptr, nullptr, T, K, img, nullptr, nullptr, s);
+                              uint8_t* ws, uint32_t* err, uint32_t nsm, cudaStream_t s) {
+    cudaError_t ce = launch_token_image(X, nullptr, nullptr, T, K, ws, nullptr, nullptr, s);
     if (ce != cudaSuccess) return ce;
-    return launch_gemm_digits(UnitW{static_cast<const uint8_t*>(units), M, unit_rows(M), K}, GemmIn{img, nullptr, 0.0f, T},
-                              GEpiStore{Y, M}, err, nsm, s);
+    GemmIn in{ws, nullptr, 0.0f, T};
+    in.part = reinterpret_cast<float*>(ws + image_part_offset(K, T));
+    in.part_floats = gemm_split_floats(nsm);
+    return launch_gemm_digits(UnitW{static_cast<const uint8_t*>(units), M, unit_rows(M), K}, in, GEpiStore{Y, M}, err,
+                              nsm, s);
 }
 
-size_t gemm_units_scratch(uint32_t K, uint32_t T) { return token_image_bytes(T, K); }
+size_t gemm_units_scratch(uint32_t K, uint32_t T, uint32_t nsm) {
+    return image_part_offset(K, T) + gemm_split_floats(nsm) * sizeof(float);
+}
 
 }  // namespace bt
 
@@ -240,7 +255,9 @@ int bt_engine_prefill(bt_engine* e, bt_kv* kv, const uint32_t* prompt, uint32_t 
     for (uint32_t done = 0; done < n_fill;) {
         const uint32_t T = std::min(n_fill - done, e->pf_cap);
         BT_CUDA_CHECK(cudaMemcpyAsync(e->pf_tok, prompt + done, sizeof(uint32_t) * T, cudaMemcpyHostToDevice, s));
-        const CacheRef cr{kv->k, kv->v, kv->rope, kv->max_seq, &kv->st->error};
+        const CacheRef cr{kv->k, kv->v, kv->rope, kv->max_seq, &kv->st->error,
+                          kv_map_flat(kv->max_seq, e->lc.head_dim),
+                          (size_t)e->lc.num_kv_heads * kv->max_seq * e->lc.head_dim};
         rc = kv->dtype == BT_KV_FP16 ? prefill_chunk_t<__half>(e, cr, T, pos0 + done, s)
                                      : prefill_chunk_t<float>(e, cr, T, pos0 + done, s);
         if (rc != BT_OK) return rc;
@@ -285,8 +302,8 @@ int bt_cuda_gemm_q8_units(const void* units, const float* X, float* Y, uint32_t 
     int dev = 0, nsm = 0;
     BT_CUDA_CHECK(cudaGetDevice(&dev));
     BT_CUDA_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
-    // token image + error flag, stream-ordered
-    const size_t img_bytes = token_image_bytes(T, K);
+    // token image and split-K partials, then the error flag; stream-ordered
+    const size_t img_bytes = gemm_units_scratch(K, T, (uint32_t)nsm);
     uint8_t* ws = nullptr;
     BT_CUDA_CHECK(cudaMallocAsync(reinterpret_cast<void**>(&ws), img_bytes + 256, s));
     uint32_t* err = reinterpret_cast<uint32_t*>(ws + img_bytes);

@@ -413,7 +413,7 @@ int bt_cuda_gemv_bench(int kind, const void* w, const float* X, float* Y, uint32
     int rc = gemv_workspace(dev, &ws);
     if (rc != BT_OK) return rc;
     uint8_t* img = nullptr;
-    if (kind == 1) BT_CUDA_CHECK(cudaMallocAsync(reinterpret_cast<void**>(&img), gemm_units_scratch(K, B), s));
+    if (kind == 1) BT_CUDA_CHECK(cudaMallocAsync(reinterpret_cast<void**>(&img), gemm_units_scratch(K, B, ws->nsm), s));
     cudaEvent_t e0, e1;
     BT_CUDA_CHECK(cudaEventCreate(&e0));
     BT_CUDA_CHECK(cudaEventCreate(&e1));

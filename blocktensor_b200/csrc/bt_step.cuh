@@ -22,6 +22,7 @@
 // through L1, where another SM's earlier line could be stale.
 #pragma once
 
+#include "bt_attn_mma.cuh"
 #include "bt_common.cuh"
 #include "bt_gemv.cuh"
 #include "bt_gemv_mma.cuh"
@@ -95,16 +96,19 @@ enum : uint32_t {
 
 // Stage timeline (a build with BT_STAGE_TRACE defined, for latency analysis):
 // after the phase part of the trace, per CTA and ring stage (the first
-// kStageTraceMax of the step): [0] the producer issues the stage's copy, [1]
-// issuer 1 sees it landed, [2] accumulator warp 5 sees its MMAs complete, [3]
-// that warp has read the results and releases the slot.
+// kStageTraceMax of the step), kStageSlots timestamps: [0] the producer issues
+// the stage's copy, [1] issuer 1 sees it landed, [2] accumulator warp 5 sees
+// its MMAs complete, [3] that warp has read the results and releases the slot,
+// [4] issuer 1 has issued and committed its MMAs of the stage, [5] accumulator
+// warp 5 starts waiting for the stage's MMAs.
 constexpr uint32_t kStageTraceMax = 2048;
+constexpr uint32_t kStageSlots = 8;
 
 __device__ __forceinline__ void stage_trace_at(const StepArgs& a, uint32_t P, uint32_t stage, uint32_t slot) {
 #ifdef BT_STAGE_TRACE
     if (a.trace && stage < kStageTraceMax)
-        a.trace[(size_t)P * gridDim.x * kTraceSlots + ((size_t)blockIdx.x * kStageTraceMax + stage) * 4 + slot] =
-            global_ns();
+        a.trace[(size_t)P * gridDim.x * kTraceSlots + ((size_t)blockIdx.x * kStageTraceMax + stage) * kStageSlots +
+                slot] = global_ns();
 #endif
 }
 
@@ -327,19 +331,32 @@ struct RowWords {
     }
 };
 
-constexpr uint32_t kAttnMaxSplits = 8;
+// Splits of a KV head's keys: about one attention item per SM, so models with
+// few KV heads (8 for the 70B shape) split each head's long cache many ways.
+constexpr uint32_t kAttnMaxSplits = 32;
+
+// Splits this step uses at context c: S_att (about one item per SM), but no
+// more than one per 64 keys, so that short caches are not cut into slivers
+// whose merge costs more than their keys.  Every CTA computes the same value;
+// the split partials of the step are laid out by it (tags tell steps apart).
+__device__ __forceinline__ uint32_t attn_splits(const StepArgs& a, uint32_t c) {
+    return max(1u, min(a.S_att, (c + 63) / 64));
+}
 
 template <int NV, int GQM, typename KVT>
 __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint32_t tid, uint8_t* img, uint32_t tag,
                            bool& ok) {
+    // grouped-query variants with head_dim 64 or 128 run the key loop on the tensor cores (bt_attn_mma.cuh)
+    constexpr bool kAttnMma = GQM > 1 && (NV == 2 || NV == 4);
     // GQM: query heads per KV head held in registers; B: keys per batch and warp
     // (half the batch when several query heads share the keys: their registers)
     constexpr int BW = 16 / RowWords<NV, KVT>::W / (GQM > 1 ? 2 : 1);
     constexpr int B = BW > 8 ? 8 : (BW < 2 ? 2 : BW);
     const uint32_t lane = tid & 31, w = tid >> 5, G = gridDim.x;
-    const uint32_t HD = a.hd, GQ = a.GQ, S = a.S_att;
+    const uint32_t HD = a.hd, GQ = a.GQ;
     const uint32_t pos = a.st->pos;
     const uint32_t c = min(pos + 1, a.max_seq);
+    const uint32_t S = attn_splits(a, c);
     const size_t layer_off = (size_t)l * a.KVH * a.max_seq * HD;
     const KVT* kl = reinterpret_cast<const KVT*>(a.kc) + layer_off;
     const KVT* vl = reinterpret_cast<const KVT*>(a.vc) + layer_off;
@@ -354,8 +371,26 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
         const uint32_t t0 = sidx * Lk, t1 = min(c, t0 + Lk);
         const KVT* kb = kl + (size_t)kvh * a.max_seq * HD + d0;
         const KVT* vb = vl + (size_t)kvh * a.max_seq * HD + d0;
+        bool on_tensor_cores = false;
+        if constexpr (kAttnMma) {
+            if (GQ <= 8 && HD == 32 * NV) {  // NV = 2 also serves head_dim < 64: those stay on the CUDA cores
+                // grouped heads on the tensor cores: the warps take 16-key tiles round robin; q's
+                // fragments in shared memory after the warps' partials
+                using GW = GqaWarp<32 * NV, KVT, true>;
+                uint4* qs = reinterpret_cast<uint4*>(scratch + ((size_t)kDigitWarps * GQ * pstride * 4 + 15) / 16 * 16);
+                GW::stage_q(qs, a.q + (size_t)kvh * GQ * HD, GQ, tid, kDigitThreads);
+                digit_sync();
+                GW st;
+                st.init(nullptr, GQ, lane, qs);
+                const size_t head_row0 = (size_t)kvh * a.max_seq;
+                auto row = [&](uint32_t t) { return (head_row0 + t) * (32 * NV); };
+                for (uint32_t k0 = t0 + 16 * w; k0 < t1; k0 += 16 * kDigitWarps) st.tile(kl, vl, k0, t1, a.scale, row);
+                st.store(wm + (size_t)w * GQ * pstride, GQ);
+                on_tensor_cores = true;
+            }
+        }
         // query heads g0 .. g0 + GQM - 1 of this KV head per pass (K/V re-read from L2 by later passes)
-        for (uint32_t g0 = 0; g0 < GQ; g0 += GQM) {
+        for (uint32_t g0 = 0; g0 < GQ && !on_tensor_cores; g0 += GQM) {
         float qv[GQM][NV], o[GQM][NV], m[GQM], ls[GQM];
 #pragma unroll
         for (int g = 0; g < GQM; ++g) {
@@ -504,7 +539,7 @@ template <typename KVT>
 __device__ void prefetch_attn_rows(const StepArgs& a, uint32_t l) {
     const uint32_t row_bytes = a.hd * (uint32_t)sizeof(KVT);
     if (row_bytes % 16) return;
-    const uint32_t c = min(a.st->pos + 1, a.max_seq), S = a.S_att;
+    const uint32_t c = min(a.st->pos + 1, a.max_seq), S = attn_splits(a, c);
     const uint32_t Lk = (c + S - 1) / S;
     const size_t layer_off = (size_t)l * a.KVH * a.max_seq * a.hd;
     for (uint32_t it = blockIdx.x; it < a.KVH * S; it += gridDim.x) {
@@ -716,6 +751,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                     tcgen05_fence_after();
                     if (ok) issue_stage(t, min(kStageTiles, gm.u1 - (gm.u0 + j * kStageTiles)), s, b, NB, a0, b0, d0);
                     umma_commit(&mma_done[s]);
+                    if (t == 0) stage_trace_at(a, P, rcount + j, 4);
                     if (++s == NS) { s = 0; ph ^= 1; }
                     b += kStageTiles;
                     while (b >= NB) b -= NB;

@@ -130,6 +130,9 @@ SIGNATURES = {
     "bt_batch_read_tokens": (_i32, [_vp, _u32, _u32, _u32, _vp]),
     "bt_batch_read_logits": (_i32, [_vp, _vp]),
     "bt_batch_step_info": (_i32, [_vp, _vp]),
+    "bt_batch_create_paged": (_i32, [_vp, _u32, _u32, _u32, _u32, _i32, C.POINTER(_vp)]),
+    "bt_batch_release": (_i32, [_vp, _u32]),
+    "bt_batch_pages": (_i32, [_vp, _vp, _vp]),
 }
 
 _LIB = None

@@ -415,7 +415,9 @@ BT_API int bt_batch_create(bt_engine* e, uint32_t n_seq, uint32_t max_seq, int k
 BT_API int bt_batch_destroy(bt_batch* b);
 /* Sequence s starts with `prompt`: positions 0 .. n_prompt - 2 are prefilled
  * (as bt_engine_prefill), and its next step processes prompt[n_prompt - 1] at
- * position n_prompt - 1.  Every sequence must be started before steps run. */
+ * position n_prompt - 1.  Every sequence of a contiguous batch must be started
+ * before steps run; in a paged batch a slot's previous sequence is released
+ * first. */
 BT_API int bt_batch_prefill(bt_batch* b, uint32_t s, const uint32_t* prompt, uint32_t n_prompt);
 /* n decode steps of every sequence (greedy), on `stream` (NULL: the engine's);
  * BT_ERR_OUT_OF_RANGE when a sequence would pass max_seq. */
@@ -428,6 +430,27 @@ BT_API int bt_batch_read_logits(bt_batch* b, float* out);
 /* Algorithmic HBM bytes of the next step: weights once, norms, one embedding
  * row per sequence, every sequence's K/V read and written. */
 BT_API int bt_batch_step_info(bt_batch* b, uint64_t* bytes);
+
+/* Paged KV for serving (replaces the reference's one contiguous single-
+ * sequence buffer per layer, runtime/src/kv_cache.cpp:6-15): a batch of n_seq
+ * sequence slots whose K/V live in one pool of n_pages pages of page_tokens
+ * positions (a power of two in [16, 4096]); a page holds every layer's
+ * [kv_heads][page_tokens][head_dim] rows, K and V in two pools.  A slot takes
+ * pages as its sequence grows (bt_batch_prefill, bt_batch_steps) and gives
+ * them back with bt_batch_release; max_seq bounds one sequence.  Slots that
+ * hold no sequence are skipped by the steps.  Results are those of
+ * bt_batch_create's contiguous caches.  A prefill or steps call that needs
+ * more pages than are free returns BT_ERR_OUT_OF_MEMORY and takes none.
+ * Calls on one batch are made from one host thread; prefill and release
+ * synchronise the engine's stream. */
+BT_API int bt_batch_create_paged(bt_engine* e, uint32_t n_seq, uint32_t max_seq, uint32_t page_tokens,
+                                 uint32_t n_pages, int kv_dtype, bt_batch** out);
+/* Ends the sequence of slot s: its pages return to the pool, the slot idles
+ * until the next bt_batch_prefill of s.  BT_ERR_INVALID_ARGUMENT on a batch
+ * without a page pool. */
+BT_API int bt_batch_release(bt_batch* b, uint32_t s);
+/* Free and total pages of the pool (0 and 0 for a contiguous batch). */
+BT_API int bt_batch_pages(bt_batch* b, uint32_t* free_pages, uint32_t* total_pages);
 
 #ifdef __cplusplus
 }

@@ -130,6 +130,33 @@ static void engine_parity(const std::string& path, const ModelConfig& cfg) {
     std::printf("engine parity (%d steps through import_btmodel + CudaBackend): %s\n", steps,
                 (bad == 0 && tok_diff == 0) ? "PASSED" : "FAILED");
 
+    // the device K/V written back into the reference KVCache equals the CPU engine's cache
+    eng.sync_to_reference(gkv);
+    const size_t n = (size_t)cfg.max_seq_len * cfg.num_kv_heads * cfg.head_dim;
+    std::vector<float> a(n), b(n);
+    int kv_bad = 0;
+    for (uint32_t l = 0; l < cfg.num_layers; ++l) {
+        for (int kv = 0; kv < 2; ++kv) {
+            (kv ? ckv.v_cache(l) : ckv.k_cache(l))->read(a.data(), n * sizeof(float), 0);
+            (kv ? gkv.v_cache(l) : gkv.k_cache(l))->read(b.data(), n * sizeof(float), 0);
+            const size_t used = (size_t)steps * cfg.num_kv_heads * cfg.head_dim;  // positions 0 .. steps - 1
+            for (size_t i = 0; i < used; ++i) kv_bad += !approx(a[i], b[i], 1e-2f);
+        }
+    }
+    CHECK(kv_bad == 0, "%d K/V elements outside 1e-2 after sync_to_reference", kv_bad);
+    std::printf("KV write-back into the reference KVCache: %s\n", kv_bad == 0 ? "PASSED" : "FAILED");
+
+    // a new KVCache (possibly at the destroyed one's address) starts from an empty device cache
+    {
+        auto fresh = std::make_unique<KVCache>(gmem, cfg.num_layers, cfg.max_seq_len, cfg.num_kv_heads, cfg.head_dim);
+        auto c0 = eng.forward_single_token(5, 0, *fresh);
+        KVCache ckv2(cmem, cfg.num_layers, cfg.max_seq_len, cfg.num_kv_heads, cfg.head_dim);
+        auto r0 = ref.forward_single_token(5, 0, ckv2);
+        int fb = 0;
+        for (size_t i = 0; i < r0.size(); ++i) fb += !approx(r0[i], c0[i], 1e-2f);
+        CHECK(fb == 0, "fresh KVCache: %d logits outside 1e-2", fb);
+    }
+
     bool caught = false;
     try { eng.forward_single_token(cfg.vocab_size, 0, gkv); } catch (const std::out_of_range&) { caught = true; }
     CHECK(caught, "token >= vocab did not throw out_of_range");
