@@ -525,7 +525,9 @@ def run_batched(args):
     cfg = synthetic.config("tinyllama-1.1b", max_seq)
     eng = bt.TransformerEngine(cfg, device=local, rope_theta=synthetic.ROPE_THETA["tinyllama-1.1b"])
     eng.generate(seed=0, sigma=0.02)
-    batch = bt.Batch(eng, per, max_seq, bt.BT_KV_FP16)
+    P = args.page_tokens
+    n_pages = sum(-(-(int(ctx[s]) + W + args.steps + args.e2e_steps + 2) // P) for s in seqs) if P else 0
+    batch = bt.Batch(eng, per, max_seq, bt.BT_KV_FP16, page_tokens=P, n_pages=n_pages)
     t0 = time.time()
     n_prompt_tokens = 0
     for i, s in enumerate(seqs):
@@ -583,7 +585,8 @@ def run_batched(args):
             "dtype": "int8", "data": "synthetic",
             "config": {"workload": f"tinyllama-1.1b-shaped batched decode, {n_total} sequences, {per} per GPU",
                        "model": "tinyllama-1.1b", "global_batch": n_total, "contexts": "uniform [128, 4096]",
-                       "kv_cache": "fp16", "parallelism": f"sequence-sharded x{world}",
+                       "kv_cache": f"fp16, paged ({P}-position pages)" if P else "fp16",
+                       "parallelism": f"sequence-sharded x{world}",
                        "l2": "inputs larger than L2 (1.16 GB of weights + every sequence's KV per step)"},
             "roofline": {"kernel": "one batched step (GEMMs + attention), per GPU", "bound": "hbm",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
@@ -602,6 +605,37 @@ def run_batched(args):
     return 0
 
 
+def run_config_only(args):
+    """One JSON line for the GEMV microbenchmark (--workload gemv: 4096 x 4096 int8, B in {1, 4,
+    16}, HBM GB/s of the tile-layout GEMV at B = 1 as the value) or the tiny decoder (--workload
+    tiny: 16-token prompt, 128 greedy steps, fp32 KV).  One GPU."""
+    import torch
+    import blocktensor_b200 as bt
+    torch.cuda.set_device(0)
+
+    def log(*a):
+        print(*a, file=sys.stderr, flush=True)
+
+    peak, peak_kind = hbm_peak()
+    if args.workload == "gemv":
+        res = c1_gemv(torch, bt, 0, log)
+        head = next(r for r in res if r["B"] == 1 and r["kernel"].startswith("tcgen05 GEMV"))
+        line = {"metric": "int8 dequant GEMV HBM GB/s (4096 x 4096, Q8_0 scales, B = 1; B = 4, 16 in rows)",
+                "value": head["GBps"], "unit": "GB/s", "n_gpus": 1, "higher_is_better": True, "dtype": "int8",
+                "data": "synthetic", "config": {"workload": "int8 GEMV 4096x4096, 16 weight copies cycled (302 MB)"},
+                "roofline": {"bound": "hbm", "achieved": head["GBps"], "peak": peak, "unit": "GB/s",
+                             "frac": head["GBps"] / peak, "peak_source": peak_kind}, "rows": res}
+    else:
+        res = c0_tiny(torch, bt, 0, log)
+        line = {"metric": "decode tokens/s (tiny Llama-style decoder, batch 1)", "value": res["tokens_per_s"],
+                "unit": "tokens/s", "n_gpus": 1, "higher_is_better": True, "dtype": "int8", "data": "synthetic",
+                "config": {"workload": "tiny decoder D288 F768 L6 H6 V32000, 16-token prompt, 128 greedy steps, fp32 KV"},
+                "roofline": {"bound": "hbm", "achieved": res["GBps"], "peak": peak, "unit": "GB/s",
+                             "frac": res["frac_of_measured_hbm"], "peak_source": peak_kind}, "detail": res}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -609,10 +643,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--model", default="llama2-7b")
-    ap.add_argument("--workload", choices=["decode", "batched"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "batched", "gemv", "tiny"], default="decode",
                     help="decode: one sequence at batch 1 (the headline); batched: TinyLlama-shaped "
                          "batched decode of --sequences sequences sharded over the ranks")
     ap.add_argument("--sequences", type=int, default=64)
+    ap.add_argument("--page-tokens", type=int, default=0,
+                    help="batched workload: K/V in a page pool of pages of this many positions (0: contiguous)")
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--profile-steps", type=int, default=0,
@@ -635,6 +671,8 @@ def main():
         return run_reference(args)
     if args.workload == "batched":
         return run_batched(args)
+    if args.workload in ("gemv", "tiny"):
+        return run_config_only(args)
     return run_ours(args)
 
 

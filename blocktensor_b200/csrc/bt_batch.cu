@@ -321,9 +321,11 @@ __global__ void __launch_bounds__(256, (HD == 64 && sizeof(KVT) == 2) ? 2 : 1) b
 
 // attn[s][h hd + d] from the splits of (s, kv head, query head): the splits'
 // maxima and sums first (lane i holds split i, i + 32, ...), then o as the
-// weighted sum over the splits in split order.  One warp per (sequence, query head).
+// weighted sum over the splits in split order.  One warp per (sequence, query
+// head).  With img (head_dim a multiple of 32: a warp's 32 values are one
+// block of the o-proj input) it also writes the o-proj GEMM's token image.
 __global__ void batch_attn_merge_kernel(const float* __restrict__ part, float* __restrict__ attn, uint32_t B,
-                                        uint32_t KVH, uint32_t GQ, uint32_t S, uint32_t hd) {
+                                        uint32_t KVH, uint32_t GQ, uint32_t S, uint32_t hd, uint8_t* img) {
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t item = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
     const uint32_t H = KVH * GQ;
@@ -366,7 +368,9 @@ __global__ void batch_attn_merge_kernel(const float* __restrict__ part, float* _
 #pragma unroll
             for (int k = 0; k < 8; ++k) acc = fmaf(ov[k], wv[k], acc);
         }
-        attn[(size_t)s * H * hd + (size_t)h * hd + d] = __fdiv_rn(acc, L);
+        const float o = __fdiv_rn(acc, L);
+        attn[(size_t)s * H * hd + (size_t)h * hd + d] = o;
+        if (img) token_terms(img, H * hd / 32, s, (h * hd + d - lane) / 32, o, lane);  // warp-uniform
     }
 }
 
@@ -435,7 +439,7 @@ int enqueue_batch_step(bt_batch* b, cudaStream_t s) {
         KVT* vl = static_cast<KVT*>(b->v) + l * b->layer_stride;
         {
             GEpiQKV<KVT> epi{b->q, kl, vl, b->map, b->rope, GemmTok{B, b->pos, b->seq_idx}, Q, KV, hd};
-            BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.qkv, QKV, unit_rows(QKV), D}, gin(b->img[0], b->ss, c.rms_norm_eps),
+            BT_CUDA_CHECK(launch_gemm_tokens(UnitW{Ld.qkv, QKV, unit_rows(QKV), D}, gin(b->img[0], b->ss, c.rms_norm_eps),
                                              epi, err, nsm, s));
         }
         BatchAttnArgs aa{b->q, kl, vl, b->map, b->pos, b->att_part, b->S, b->kps, c.num_kv_heads, GQ, hd,
@@ -444,21 +448,23 @@ int enqueue_batch_step(bt_batch* b, cudaStream_t s) {
         {
             const uint32_t items = B * c.num_heads;
             g_launches.fetch_add(1, std::memory_order_relaxed);
+            // the merge writes the o-proj input's token image too when a head is whole 32-blocks
+            uint8_t* oimg = hd % 32 == 0 ? b->img[1] : nullptr;
             batch_attn_merge_kernel<<<(items + 7) / 8, 256, 0, s>>>(b->att_part, b->attn, B, c.num_kv_heads, GQ, b->S,
-                                                                   hd);
+                                                                   hd, oimg);
             BT_CUDA_CHECK(cudaGetLastError());
+            if (!oimg) BT_CUDA_CHECK(launch_token_image(b->attn, nullptr, nullptr, B, Q, b->img[1], nullptr, nullptr, s));
         }
-        BT_CUDA_CHECK(launch_token_image(b->attn, nullptr, nullptr, B, Q, b->img[1], nullptr, nullptr, s));
-        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.o, D, unit_rows(D), Q}, gin(b->img[1], nullptr, 0.0f),
+        BT_CUDA_CHECK(launch_gemm_tokens(UnitW{Ld.o, D, unit_rows(D), Q}, gin(b->img[1], nullptr, 0.0f),
                                          GEpiResidual{b->x, Ld.ffn_norm, b->img[0], b->ss, nullptr, D}, err, nsm, s));
-        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.gu, 2 * F, unit_rows(2 * F), D}, gin(b->img[0], b->ss, c.rms_norm_eps),
+        BT_CUDA_CHECK(launch_gemm_tokens(UnitW{Ld.gu, 2 * F, unit_rows(2 * F), D}, gin(b->img[0], b->ss, c.rms_norm_eps),
                                          GEpiSwiGLU{b->act, b->img[1], F}, err, nsm, s));
         const float* wn = l + 1 < L ? e->layers[l + 1].attn_norm : e->out_norm;
-        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.d, D, unit_rows(D), F}, gin(b->img[1], nullptr, 0.0f),
+        BT_CUDA_CHECK(launch_gemm_tokens(UnitW{Ld.d, D, unit_rows(D), F}, gin(b->img[1], nullptr, 0.0f),
                                          GEpiResidual{b->x, wn, b->img[0], b->ss, nullptr, D}, err, nsm, s));
     }
     const uint32_t nob = unit_rows(V) / 32;
-    BT_CUDA_CHECK(launch_gemm_digits(UnitW{e->head, V, unit_rows(V), D}, gin(b->img[0], b->ss, c.rms_norm_eps),
+    BT_CUDA_CHECK(launch_gemm_tokens(UnitW{e->head, V, unit_rows(V), D}, gin(b->img[0], b->ss, c.rms_norm_eps),
                                      GEpiLogits{b->logits, b->am_val, b->am_idx, V, nob}, err, nsm, s));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     batch_finish_kernel<<<(B + 7) / 8, 256, 0, s>>>(b->am_val, b->am_idx, nob, B, b->max_seq, b->pos, b->cur,

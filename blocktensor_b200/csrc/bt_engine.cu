@@ -107,9 +107,11 @@ int plan_step(bt_engine* e) {
     if (qd(c) > kmax) kmax = qd(c);
     const size_t img_bytes = mma_digit_bytes(kmax);  // digits + block factors
     size_t scratch = img_bytes;
-    // attention: the warps' partials [9][GQ][hd + 2], then (grouped heads) q's tensor-core
-    // fragments, 16 bytes per lane and k-step, 16-byte aligned
-    const size_t attn = ((size_t)kDigitWarps * GQ * (hd + 2) * 4 + 15) / 16 * 16 + (size_t)32 * (hd / 8) * 16;
+    // attention: the warps' partials [9][GQ][hd + 2], then, 16-byte aligned, either q's
+    // tensor-core fragments (grouped heads: 16 bytes per lane and k-step) or, after the key
+    // loop, the split merge's (m, l, weight) of every head and split and the heads' totals
+    const size_t frag = (size_t)32 * (hd / 8) * 16, merge = ((size_t)GQ * kAttnMaxSplits * 3 + GQ) * 4;
+    const size_t attn = ((size_t)kDigitWarps * GQ * (hd + 2) * 4 + 15) / 16 * 16 + (frag > merge ? frag : merge);
     if (attn > scratch) scratch = attn;
     scratch = (scratch + 127) / 128 * 128;
     const size_t budget = 220 * 1024;

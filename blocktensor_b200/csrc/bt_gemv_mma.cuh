@@ -30,8 +30,10 @@
 // stages into an mbarrier ring; weights never depend on the previous kernel,
 // so under programmatic dependent launch the ring fills while the previous
 // kernel drains); warps 1-4 issue the MMAs, warp 1+t for tiles t and t+4 of
-// every stage (one thread issuing tcgen05.mma + commit spends ~390 cycles per
-// MMA, so a single issuer could not keep up with HBM); warps 5-8 read the
+// every stage (one thread issuing back-to-back tcgen05.mma spends ~230 cycles
+// per MMA whatever N up to 64 and however often it commits; four issuers reach
+// ~58 cycles per MMA together, eight ~39 -- measured with a probe kernel -- so
+// a single issuer could not keep up with HBM); warps 5-8 read the
 // digit sums from tensor memory (warp w reads TMEM lanes 32 (w%4) .. +31, all
 // eight tiles of a stage with one load) and accumulate; warp 9 finishes each
 // row tile (cross-CTA merge, epilogue).  Stages are 36 KB because every stage
@@ -563,6 +565,7 @@ __device__ __forceinline__ void acc_stages(uint32_t u0, uint32_t u1, uint32_t NB
                 if (++b == NB) { b = 0; ++g; }
             }
         }
+        hook(j, 6);
     }
 }
 

@@ -184,7 +184,7 @@ int prefill_chunk_t(bt_engine* e, const CacheRef& kv, uint32_t T, uint32_t pos0,
         // qkv + RoPE + K/V append
         {
             GEpiQKV<KVT> epi{e->pf_q, kl, vl, kv.map, kv.rope, GemmTok{T, e->pf_pos, nullptr}, Q, KV, hd};
-            BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.qkv, QKV, unit_rows(QKV), D},
+            BT_CUDA_CHECK(launch_gemm_tokens(UnitW{Ld.qkv, QKV, unit_rows(QKV), D},
                                              gin(e->pf_img[0], e->pf_ss, c.rms_norm_eps), epi, err, nsm, s));
         }
         // causal attention over the cache, then the o-proj input's token image
@@ -192,17 +192,17 @@ int prefill_chunk_t(bt_engine* e, const CacheRef& kv, uint32_t T, uint32_t pos0,
                                                c.num_heads / c.num_kv_heads, hd, kv.map, scale, s));
         BT_CUDA_CHECK(launch_token_image(e->pf_attn, nullptr, nullptr, T, Q, e->pf_img[1], nullptr, nullptr, s));
         // o-proj + residual; token image of x * ffn_norm
-        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.o, D, unit_rows(D), Q}, gin(e->pf_img[1], nullptr, 0.0f),
+        BT_CUDA_CHECK(launch_gemm_tokens(UnitW{Ld.o, D, unit_rows(D), Q}, gin(e->pf_img[1], nullptr, 0.0f),
                                          GEpiResidual{e->pf_x, Ld.ffn_norm, e->pf_img[0], e->pf_ss, nullptr, D}, err,
                                          nsm, s));
         // gate/up + SwiGLU; token image of act
-        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.gu, 2 * F, unit_rows(2 * F), D},
+        BT_CUDA_CHECK(launch_gemm_tokens(UnitW{Ld.gu, 2 * F, unit_rows(2 * F), D},
                                          gin(e->pf_img[0], e->pf_ss, c.rms_norm_eps),
                                          GEpiSwiGLU{e->pf_act, e->pf_img[1], F}, err, nsm, s));
         // down + residual; token image of x * the next layer's attn_norm (the last layer's output
         // is not used: the decode step processes the final prompt token)
         const float* wn = l + 1 < L ? e->layers[l + 1].attn_norm : e->out_norm;
-        BT_CUDA_CHECK(launch_gemm_digits(UnitW{Ld.d, D, unit_rows(D), F}, gin(e->pf_img[1], nullptr, 0.0f),
+        BT_CUDA_CHECK(launch_gemm_tokens(UnitW{Ld.d, D, unit_rows(D), F}, gin(e->pf_img[1], nullptr, 0.0f),
                                          GEpiResidual{e->pf_x, wn, e->pf_img[0], e->pf_ss, nullptr, D}, err, nsm,
                                          s));
     }
@@ -222,7 +222,7 @@ cudaError_t gemm_units_launch(const void* units, const float* X, float* Y, uint3
     GemmIn in{ws, nullptr, 0.0f, T};
     in.part = reinterpret_cast<float*>(ws + image_part_offset(K, T));
     in.part_floats = gemm_split_floats(nsm);
-    return launch_gemm_digits(UnitW{static_cast<const uint8_t*>(units), M, unit_rows(M), K}, in, GEpiStore{Y, M}, err,
+    return launch_gemm_tokens(UnitW{static_cast<const uint8_t*>(units), M, unit_rows(M), K}, in, GEpiStore{Y, M}, err,
                               nsm, s);
 }
 

@@ -156,6 +156,15 @@ __device__ __forceinline__ void umma_s8(uint32_t d_tmem, uint64_t a, uint64_t b,
         : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, f16 x f16 -> f32 (one thread issues).
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // The mbarrier receives one arrival when all earlier MMAs of this thread are complete.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

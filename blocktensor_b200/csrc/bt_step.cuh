@@ -100,7 +100,7 @@ enum : uint32_t {
 // the stage's copy, [1] issuer 1 sees it landed, [2] accumulator warp 5 sees
 // its MMAs complete, [3] that warp has read the results and releases the slot,
 // [4] issuer 1 has issued and committed its MMAs of the stage, [5] accumulator
-// warp 5 starts waiting for the stage's MMAs.
+// warp 5 starts waiting for the stage's MMAs, [6] it has added the stage's sums.
 constexpr uint32_t kStageTraceMax = 2048;
 constexpr uint32_t kStageSlots = 8;
 
@@ -458,9 +458,13 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
         }
         }
         digit_sync();
-        // CTA partial of this split.  The CTA of split 0 keeps its own and merges the others (:148-184),
-        // which publish theirs as (tag, value) words and move on.
+        // CTA partial of this split (the warps' (m, l, o) merged).  The splits other than 0 publish
+        // theirs as (tag, value) words and move on; split 0's CTA keeps its own (o in warp 0's row of
+        // wm, which only this element's thread reads; m and l in mls) and merges the others.
         uint64_t* pg = a.att_part + (size_t)kvh * GQ * S * pstride;
+        // [GQ][S][3] (m, l, weight) of the splits, then [GQ] totals, after the warps' partials
+        float* mls = reinterpret_cast<float*>(scratch + ((size_t)kDigitWarps * GQ * pstride * 4 + 15) / 16 * 16);
+        float* ltot = mls + (size_t)GQ * S * 3;
         for (uint32_t e = tid; e < GQ * HD; e += kDigitThreads) {
             const uint32_t g = e / HD, d = e % HD;
             float M = -INFINITY;
@@ -486,46 +490,82 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
                 }
                 continue;
             }
-            // split 0: add the other splits' (m, l, o[d]) in split order (online rescaling), once all
-            // their tags are this phase's; a poll that finds one missing starts over
-            const bool own = lsum > 0.0f;
-            float ltot = own ? lsum : 0.0f, atot = own ? acc : 0.0f;
-            const uint64_t t0 = global_ns();
-            while (ok) {
-                bool have = true;
-                float Mr = own ? M : -INFINITY, lr = own ? lsum : 0.0f, ar = own ? acc : 0.0f;
-                for (uint32_t s = 1; s < S; ++s) {
-                    const uint64_t* src = pg + ((size_t)g * S + s) * pstride;
-                    const uint64_t wm_ = ld_relaxed_u64(src), wl = ld_relaxed_u64(src + 1), wo = ld_relaxed_u64(src + 2 + d);
-                    have = have && (uint32_t)(wm_ >> 32) == tag && (uint32_t)(wl >> 32) == tag && (uint32_t)(wo >> 32) == tag;
-                    const float ms = __uint_as_float((uint32_t)wm_), ls_ = __uint_as_float((uint32_t)wl);
-                    const float os = __uint_as_float((uint32_t)wo);
-                    if (!(ls_ > 0.0f)) continue;
-                    if (ms > Mr) {
-                        const float r = expf(Mr - ms);  // 0 while nothing is accumulated (Mr = -inf)
-                        lr = fmaf(lr, r, ls_);
-                        ar = fmaf(ar, r, os);
-                        Mr = ms;
-                    } else {
-                        const float f = expf(ms - Mr);
-                        lr = fmaf(ls_, f, lr);
-                        ar = fmaf(os, f, ar);
-                    }
-                }
-                if (have) {
-                    ltot = lr;
-                    atot = ar;
-                    break;
-                }
-                if (global_ns() - t0 > kWaitNs) {
-                    atomicExch(&a.st->error, 1u);
-                    ok = false;
-                }
+            wm[(size_t)g * pstride + 2 + d] = acc;  // warp 0's row: read by this thread only
+            if (d == 0) {
+                mls[(size_t)g * S * 3] = M;
+                mls[(size_t)g * S * 3 + 1] = lsum;
             }
-            const float o = __fdiv_rn(atot, ltot);
-            a.attn[(size_t)(kvh * GQ + g) * HD + d] = o;
-            // digits of the o-proj input: this warp holds the 32 elements of one block
-            if (img) warp_block_digits(img, a.xstride, (kvh * GQ * HD + e) >> 5, o, lane);
+        }
+        if (sidx == 0) {
+            digit_sync();
+            // every other split's (m, l) of every head, polled in parallel (bounded)
+            const uint64_t tw = global_ns();
+            for (uint32_t i = tid; i < GQ * (S - 1); i += kDigitThreads) {
+                const uint32_t g = i / (S - 1), sp = 1 + i % (S - 1);
+                const uint64_t* src = pg + ((size_t)g * S + sp) * pstride;
+                uint64_t wmv = ld_relaxed_u64(src), wl = ld_relaxed_u64(src + 1);
+                while (ok && ((uint32_t)(wmv >> 32) != tag || (uint32_t)(wl >> 32) != tag)) {
+                    if (global_ns() - tw > kWaitNs) {
+                        atomicExch(&a.st->error, 1u);
+                        ok = false;
+                        break;
+                    }
+                    wmv = ld_relaxed_u64(src);
+                    wl = ld_relaxed_u64(src + 1);
+                }
+                mls[((size_t)g * S + sp) * 3] = __uint_as_float((uint32_t)wmv);
+                mls[((size_t)g * S + sp) * 3 + 1] = __uint_as_float((uint32_t)wl);
+            }
+            digit_sync();
+            // per head: the maximum over the splits that saw keys, each split's weight, the total
+            for (uint32_t g = tid; g < GQ; g += kDigitThreads) {
+                float* mg = mls + (size_t)g * S * 3;
+                float Mx = -INFINITY;
+                for (uint32_t sp = 0; sp < S; ++sp)
+                    if (mg[3 * sp + 1] > 0.0f) Mx = fmaxf(Mx, mg[3 * sp]);
+                float L = 0.0f;
+                for (uint32_t sp = 0; sp < S; ++sp) {
+                    const float w = mg[3 * sp + 1] > 0.0f ? expf(mg[3 * sp] - Mx) : 0.0f;
+                    mg[3 * sp + 2] = w;
+                    L = fmaf(mg[3 * sp + 1], w, L);
+                }
+                ltot[g] = L;
+            }
+            digit_sync();
+            // elements: o = (sum over the splits, in split order, of weight * o_split) / total
+            for (uint32_t e = tid; e < GQ * HD; e += kDigitThreads) {
+                const uint32_t g = e / HD, d = e % HD;
+                const float* mg = mls + (size_t)g * S * 3;
+                float acc = mg[2] * wm[(size_t)g * pstride + 2 + d];
+                for (uint32_t s0 = 1; s0 < S; s0 += 8) {
+                    float ov[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const uint32_t sp = s0 + k;
+                        ov[k] = 0.0f;
+                        if (sp < S) {
+                            const uint64_t* src = pg + ((size_t)g * S + sp) * pstride + 2 + d;
+                            uint64_t w = ld_relaxed_u64(src);
+                            while (ok && (uint32_t)(w >> 32) != tag) {
+                                if (global_ns() - tw > kWaitNs) {
+                                    atomicExch(&a.st->error, 1u);
+                                    ok = false;
+                                    break;
+                                }
+                                w = ld_relaxed_u64(src);
+                            }
+                            ov[k] = __uint_as_float((uint32_t)w);
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if (s0 + k < S) acc = fmaf(mg[3 * (s0 + k) + 2], ov[k], acc);
+                }
+                const float o = __fdiv_rn(acc, ltot[g]);
+                a.attn[(size_t)(kvh * GQ + g) * HD + d] = o;
+                // digits of the o-proj input: this warp holds the 32 elements of one block
+                if (img) warp_block_digits(img, a.xstride, (kvh * GQ * HD + e) >> 5, o, lane);
+            }
         }
         digit_sync();  // shared memory reused by the next item
     }
