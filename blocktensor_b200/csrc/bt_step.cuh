@@ -458,9 +458,13 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
         }
         }
         digit_sync();
-        // CTA partial of this split (the warps' (m, l, o) merged).  The splits other than 0 publish
-        // theirs as (tag, value) words and move on; split 0's CTA keeps its own (o in warp 0's row of
-        // wm, which only this element's thread reads; m and l in mls) and merges the others.
+        // CTA partial of this split (the warps' (m, l, o) merged).  When every CTA holds at most one
+        // item (KVH S <= G), all splits publish theirs as (tag, value) words and then all of them
+        // merge: split s's CTA takes the 32-element blocks s, s + S, ... of the KV head's query
+        // outputs, so no single CTA merges every split.  Otherwise the splits other than 0 publish
+        // and move on, and split 0's CTA keeps its own (o in warp 0's row of wm, which only this
+        // element's thread reads; m and l in mls) and merges the others.
+        const bool spread = a.KVH * S <= G;
         uint64_t* pg = a.att_part + (size_t)kvh * GQ * S * pstride;
         // [GQ][S][3] (m, l, weight) of the splits, then [GQ] totals, after the warps' partials
         float* mls = reinterpret_cast<float*>(scratch + ((size_t)kDigitWarps * GQ * pstride * 4 + 15) / 16 * 16);
@@ -481,7 +485,7 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
                     acc = fmaf(p[2 + d], f, acc);
                 }
             }
-            if (sidx != 0) {
+            if (sidx != 0 || spread) {
                 uint64_t* dst = pg + ((size_t)g * S + sidx) * pstride;
                 st_relaxed_u64(dst + 2 + d, tagw | __float_as_uint(acc));
                 if (d == 0) {
@@ -496,7 +500,65 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
                 mls[(size_t)g * S * 3 + 1] = lsum;
             }
         }
-        if (sidx == 0) {
+        if (spread) {
+            // this split's blocks of the KV head's GQ HD outputs, one warp per block, lane = element;
+            // (m, l, o) of every split added in split order with online rescaling (:148-184)
+            const uint32_t nblk = (GQ * HD + 31) / 32;
+            const uint64_t tw = global_ns();
+            for (uint32_t bk = sidx + S * w; bk < nblk; bk += S * kDigitWarps) {
+                const uint32_t e = bk * 32 + lane;
+                const bool valid = e < GQ * HD;
+                const uint32_t g = valid ? e / HD : 0, d = valid ? e % HD : 0;
+                const uint64_t* src = pg + (size_t)g * S * pstride;
+                float Mr = -INFINITY, lr = 0.0f, ar = 0.0f;
+                for (uint32_t s0 = 0; s0 < S; s0 += 4) {
+                    uint64_t wmv[4], wl[4], wo[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        wmv[k] = wl[k] = wo[k] = (uint64_t)tag << 32;  // splits past S: l = 0, skipped
+                        if (valid && s0 + k < S) {
+                            const uint64_t* q = src + (size_t)(s0 + k) * pstride;
+                            wmv[k] = ld_relaxed_u64(q);
+                            wl[k] = ld_relaxed_u64(q + 1);
+                            wo[k] = ld_relaxed_u64(q + 2 + d);
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        if (!(valid && s0 + k < S)) continue;
+                        const uint64_t* q = src + (size_t)(s0 + k) * pstride;
+                        while (ok && ((uint32_t)(wmv[k] >> 32) != tag || (uint32_t)(wl[k] >> 32) != tag ||
+                                      (uint32_t)(wo[k] >> 32) != tag)) {
+                            if (global_ns() - tw > kWaitNs) {
+                                atomicExch(&a.st->error, 1u);
+                                ok = false;
+                                break;
+                            }
+                            wmv[k] = ld_relaxed_u64(q);
+                            wl[k] = ld_relaxed_u64(q + 1);
+                            wo[k] = ld_relaxed_u64(q + 2 + d);
+                        }
+                        const float ms = __uint_as_float((uint32_t)wmv[k]), ls_ = __uint_as_float((uint32_t)wl[k]);
+                        const float os = __uint_as_float((uint32_t)wo[k]);
+                        if (!(ls_ > 0.0f)) continue;
+                        if (ms > Mr) {
+                            const float r = expf(Mr - ms);  // 0 while nothing is accumulated (Mr = -inf)
+                            lr = fmaf(lr, r, ls_);
+                            ar = fmaf(ar, r, os);
+                            Mr = ms;
+                        } else {
+                            const float f = expf(ms - Mr);
+                            lr = fmaf(ls_, f, lr);
+                            ar = fmaf(os, f, ar);
+                        }
+                    }
+                }
+                const float o = __fdiv_rn(ar, lr);
+                if (valid) a.attn[(size_t)(kvh * GQ) * HD + e] = o;
+                // digits of the o-proj input: the warp's 32 elements are one block when HD % 32 == 0
+                if (img) warp_block_digits(img, a.xstride, (kvh * GQ * HD) / 32 + bk, o, lane);
+            }
+        } else if (sidx == 0) {
             digit_sync();
             // every other split's (m, l) of every head, polled in parallel (bounded)
             const uint64_t tw = global_ns();
