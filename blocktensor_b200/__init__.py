@@ -395,6 +395,12 @@ class Batch:
         call("bt_batch_read_tokens", self._h, s, pos0, n, out.ctypes.data)
         return out
 
+    def read_current(self) -> np.ndarray:
+        """Every sequence's newest token, one copy (bt_batch_read_current)."""
+        out = np.zeros(self.n_seq, np.uint32)
+        call("bt_batch_read_current", self._h, out.ctypes.data)
+        return out
+
     def read_logits(self) -> np.ndarray:
         out = np.zeros((self.n_seq, self.engine.config.vocab_size), np.float32)
         call("bt_batch_read_logits", self._h, out.ctypes.data)

@@ -831,6 +831,19 @@ int bt_batch_read_tokens(bt_batch* b, uint32_t s, uint32_t pos0, uint32_t n, uin
     return BT_OK;
 }
 
+int bt_batch_read_current(bt_batch* b, uint32_t* out) {
+    int rc = check_batch(b);
+    if (rc != BT_OK) return rc;
+    if (!out) return fail(BT_ERR_INVALID_ARGUMENT, "bt_batch_read_current: null output");
+    DeviceGuard guard(b->e->device);
+    BT_CUDA_CHECK(cudaStreamSynchronize(b->e->stream));
+    BT_CUDA_CHECK(cudaMemcpy(out, b->cur, sizeof(uint32_t) * b->n_seq, cudaMemcpyDeviceToHost));
+    uint32_t flag = 0;
+    BT_CUDA_CHECK(cudaMemcpy(&flag, b->err, sizeof(flag), cudaMemcpyDeviceToHost));
+    if (flag) return fail(BT_ERR_DEVICE_TIMEOUT, "batch decode: a device wait timed out");
+    return BT_OK;
+}
+
 int bt_batch_read_logits(bt_batch* b, float* out) {
     int rc = check_batch(b);
     if (rc != BT_OK) return rc;

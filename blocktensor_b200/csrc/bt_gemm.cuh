@@ -32,10 +32,11 @@
 // Work: a unit is (row tile g, token group tg, K-split ks); CTAs take units
 // round robin, consecutive units sharing a row tile.  Warp 0 streams the
 // unit's weight tiles and token tiles in stages of 4 blocks (one mbarrier
-// ring); warps 1-2 convert the weight tiles to fp16 (a ring of 8 converted
-// tiles); warps 3-6 issue the four MMAs of a block (issuer i takes blocks i,
-// i + 4, ...; one thread spends ~230 cycles per MMA) into one of 8
-// tensor-memory slots of 64 columns; 8 reader warps (4 lane quarters x 2
+// ring); warps 1-4 convert the weight tiles to fp16 (a ring of 6 converted
+// tiles; converting a 4 KB tile takes one warp ~0.5 us); warps 5-7 issue the
+// four MMAs of a block (issuer i takes blocks i, i + 3, ...; one thread spends
+// ~0.3 us on a block's four MMAs and two commits) into one of 8
+// tensor-memory slots of 64 columns; 8 reader warps 8-15 (4 lane quarters x 2
 // token halves of 32) read the slot, accumulate 32 tokens x their 32 rows in
 // registers and, after the unit's last block, run the epilogue on them, 16
 // tokens at a time (a warp's 32 rows are one 32-element block of the output,
@@ -60,12 +61,12 @@ constexpr uint32_t kGStageBlocks = 4;
 constexpr uint32_t kGStageW = kGStageBlocks * kTileBytes;  // weight part of a stage
 constexpr uint32_t kGStageBytes = kGStageW + kGStageBlocks * kGDTile;  // 52224
 constexpr uint32_t kGSlots = 8;                           // tensor-memory slots of kGTok columns (all 512)
-constexpr uint32_t kGA16Slots = 8;                        // converted weight tiles in flight
-constexpr int kGConv0 = 1, kGConvs = 2;                   // converter warps 1-2
-constexpr int kGIssuer0 = 3, kGIssuers = 4;               // issuer warps 3-6
-constexpr int kGReader0 = 7, kGReaders = 8;               // reader warps 7-14
-constexpr int kGThreads = 32 * (kGReader0 + kGReaders);   // 480
-constexpr uint32_t kGMaxStages = 2;
+constexpr uint32_t kGA16Slots = 6;                        // converted weight tiles in flight
+constexpr int kGConv0 = 1, kGConvs = 4;                   // converter warps 1-4
+constexpr int kGIssuer0 = 5, kGIssuers = 3;               // issuer warps 5-7
+constexpr int kGReader0 = 8, kGReaders = 8;               // reader warps 8-15
+constexpr int kGThreads = 32 * (kGReader0 + kGReaders);   // 512
+constexpr uint32_t kGMaxStages = 3;
 constexpr uint32_t kGSmem = kGMaxStages * kGStageBytes + kGA16Slots * kGA16 + 2 * 16 * 64 * 4;  // + SwiGLU exchange
 
 // Instruction descriptor: D f32, A and B f16, both K-major, N = 64, M = 128.
@@ -76,8 +77,9 @@ inline __host__ __device__ size_t token_image_bytes(uint32_t T, uint32_t K) {
     return (size_t)token_groups(T) * (K / 32) * kGDTile;
 }
 
-// 2^e for e in [-126, 127] and beyond, as a product of two exact powers of two.
-__device__ __forceinline__ float scale_pow2(float v, int e) { return __fmul_rn(__fmul_rn(v, ldexpf(1.0f, e / 2)), ldexpf(1.0f, e - e / 2)); }
+// v * 2^e for e in [-149, 149]: two exact power-of-two factors (each within the
+// normal range), so the product is exact unless it underflows.
+__device__ __forceinline__ float scale_pow2(float v, int e) { return __fmul_rn(__fmul_rn(v, pow2i(e / 2)), pow2i(e - e / 2)); }
 
 // The fp16 terms of block b of token t in a token image of NB blocks per token:
 // warp-uniform call, lane i holding element 32 b + i.  The block's max |p| is
@@ -91,7 +93,10 @@ __device__ __forceinline__ void token_terms(uint8_t* img, uint32_t NB, uint32_t 
     int e = 0;
     if (am > 0.0f && finite) {
         int ex;  // am = fr * 2^ex, fr in [0.5, 1)
-        frexpf(am, &ex);
+        if (am >= 1.17549435e-38f)
+            ex = ((__float_as_int(am) >> 23) & 255) - 126;
+        else
+            frexpf(am, &ex);
         e = 15 - ex;  // am * 2^e in [2^14, 2^15)
         if (e > 149) e = 149;
     }
@@ -376,7 +381,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tokens_kernel(UnitW W, Gemm
     }
 
     if (warp < kGIssuer0) {
-        // ---------------- converters: converter c takes the blocks j with j % 2 == c; each lane
+        // ---------------- converters: converter c takes the blocks j with j % 4 == c; each lane
         // turns 8 of the tile's 256 16-byte int8 chunks into fp16 (int8 + 128 as the low byte of
         // 0x6400 = 1024, minus 1152: exact)
         const uint32_t cv = warp - kGConv0;
@@ -430,7 +435,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tokens_kernel(UnitW W, Gemm
     }
 
     if (warp < kGReader0) {
-        // ---------------- issuers: issuer i takes the blocks j with j % 4 == i
+        // ---------------- issuers: issuer i takes the blocks j with j % 3 == i
         const uint32_t i = warp - kGIssuer0;
         if (lane == 0) {
             bool ok = true;
@@ -588,14 +593,20 @@ __global__ void __launch_bounds__(128) gemm_reduce_kernel(UnitW W, GemmIn in, Ep
     float v[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = 0.0f;
-    // split by split, the 16 tokens' loads of a split in flight together
-    for (uint32_t ks = 0; ks < in.KS; ++ks) {
-        const float* pk = in.part + ((size_t)ks * in.T + tok0) * W.Mp + r;
-        float t[16];
+    // four splits at a time, the 16 tokens' loads of all four in flight together; added in split order
+    for (uint32_t ks0 = 0; ks0 < in.KS; ks0 += 4) {
+        float t[4][16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) t[i] = (uint32_t)i < nvalid ? __ldcg(pk + (size_t)i * W.Mp) : 0.0f;
+        for (int k = 0; k < 4; ++k) {
+            const float* pk = in.part + ((size_t)(ks0 + k) * in.T + tok0) * W.Mp + r;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] += t[i];
+            for (int i = 0; i < 16; ++i)
+                t[k][i] = (ks0 + k < in.KS && (uint32_t)i < nvalid) ? __ldcg(pk + (size_t)i * W.Mp) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] += t[k][i];
     }
     if (in.ss) scale_by_token_inv(v, in.ss, NB, W.K, in.eps, tok0, nvalid, lane);
     auto bar = []() { __syncthreads(); };

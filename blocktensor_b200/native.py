@@ -128,6 +128,7 @@ SIGNATURES = {
     "bt_batch_prefill": (_i32, [_vp, _u32, _vp, _u32]),
     "bt_batch_steps": (_i32, [_vp, _u32, _vp]),
     "bt_batch_read_tokens": (_i32, [_vp, _u32, _u32, _u32, _vp]),
+    "bt_batch_read_current": (_i32, [_vp, _vp]),
     "bt_batch_read_logits": (_i32, [_vp, _vp]),
     "bt_batch_step_info": (_i32, [_vp, _vp]),
     "bt_batch_create_paged": (_i32, [_vp, _u32, _u32, _u32, _u32, _i32, C.POINTER(_vp)]),

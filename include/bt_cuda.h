@@ -425,6 +425,10 @@ BT_API int bt_batch_steps(bt_batch* b, uint32_t n, void* stream);
 /* Token consumed by sequence s at positions pos0 .. pos0 + n - 1 (prompt, then
  * greedy tokens); BT_ERR_DEVICE_TIMEOUT when a device wait gave up. */
 BT_API int bt_batch_read_tokens(bt_batch* b, uint32_t s, uint32_t pos0, uint32_t n, uint32_t* out);
+/* Each sequence's newest token (the greedy token of its last step; for a
+ * sequence that has not stepped, its last prompt token), [n_seq] in one copy:
+ * the per-step read-back of a serving loop.  BT_ERR_DEVICE_TIMEOUT as above. */
+BT_API int bt_batch_read_current(bt_batch* b, uint32_t* out);
 /* Logits of every sequence's last step, [n_seq][vocab] fp32 (host). */
 BT_API int bt_batch_read_logits(bt_batch* b, float* out);
 /* Algorithmic HBM bytes of the next step: weights once, norms, one embedding

@@ -39,6 +39,8 @@ def run_batch(cuda, eng, prompts, n_gen, max_seq, kv_dtype):
         b.prefill(s, p)
     b.steps(n_gen)
     toks = [b.read_tokens(s, 0, len(p) + n_gen) for s, p in enumerate(prompts)]
+    # the serving read-back: every sequence's newest token in one copy
+    assert np.array_equal(b.read_current(), np.array([t[-1] for t in toks], np.uint32))
     logits = b.read_logits()
     b.close()
     return toks, logits
