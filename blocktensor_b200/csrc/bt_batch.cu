@@ -115,6 +115,8 @@ struct GEpiLogits {
 __global__ void batch_finish_kernel(const float* __restrict__ pv, const uint32_t* __restrict__ pi, uint32_t nob,
                                     uint32_t n_seq, uint32_t max_seq, uint32_t* pos, uint32_t* cur,
                                     const uint32_t* n_fixed, uint32_t* last_am, uint32_t* tok_hist) {
+    pdl_trigger();
+    pdl_wait();  // the head GEMM's argmax partials
     const uint32_t s = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (s >= n_seq) return;
     float bv = -INFINITY;
@@ -183,6 +185,8 @@ struct BatchAttnArgs {
 
 template <int NV, int GQM, typename KVT>
 __global__ void __launch_bounds__(256) batch_attn_kernel(BatchAttnArgs a) {
+    pdl_trigger();
+    pdl_wait();  // q and the appended K/V rows of the qkv GEMM
     extern __shared__ float wm[];  // [8 warps][GQ][hd + 2]
     constexpr int BW = 16 / RowWords<NV, KVT>::W / (GQM > 1 ? 2 : 1);
     constexpr int B = BW > 8 ? 8 : (BW < 2 ? 2 : BW);
@@ -279,6 +283,8 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(BatchAttnArgs a) {
 // warps take 16-key tiles of the split round robin.
 template <int HD, typename KVT>
 __global__ void __launch_bounds__(256, (HD == 64 && sizeof(KVT) == 2) ? 2 : 1) batch_attn_mma_kernel(BatchAttnArgs a) {
+    pdl_trigger();
+    pdl_wait();  // q and the appended K/V rows of the qkv GEMM
     extern __shared__ float wm[];  // [8 warps][GQ][HD + 2]
     const uint32_t lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const uint32_t sp = blockIdx.x, kvh = blockIdx.y, s = blockIdx.z;
@@ -326,6 +332,8 @@ __global__ void __launch_bounds__(256, (HD == 64 && sizeof(KVT) == 2) ? 2 : 1) b
 // block of the o-proj input) it also writes the o-proj GEMM's token image.
 __global__ void batch_attn_merge_kernel(const float* __restrict__ part, float* __restrict__ attn, uint32_t B,
                                         uint32_t KVH, uint32_t GQ, uint32_t S, uint32_t hd, uint8_t* img) {
+    pdl_trigger();
+    pdl_wait();  // the splits' partials
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t item = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
     const uint32_t H = KVH * GQ;
@@ -384,9 +392,7 @@ cudaError_t launch_batch_attn_t(const BatchAttnArgs& a, uint32_t B, cudaStream_t
         const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-    kern<<<dim3(a.S, a.KVH, B), 256, smem, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(a.S, a.KVH, B), dim3(256), smem, st, true, a);
 }
 
 template <int HD, typename KVT>
@@ -398,9 +404,7 @@ cudaError_t launch_batch_attn_mma(const BatchAttnArgs& a, uint32_t B, cudaStream
         const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-    kern<<<dim3(a.S, a.KVH, B), 256, smem, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(a.S, a.KVH, B), dim3(256), smem, st, true, a);
 }
 
 template <typename KVT>
@@ -447,12 +451,10 @@ int enqueue_batch_step(bt_batch* b, cudaStream_t s) {
         BT_CUDA_CHECK(launch_batch_attn<KVT>(aa, B, s));
         {
             const uint32_t items = B * c.num_heads;
-            g_launches.fetch_add(1, std::memory_order_relaxed);
             // the merge writes the o-proj input's token image too when a head is whole 32-blocks
             uint8_t* oimg = hd % 32 == 0 ? b->img[1] : nullptr;
-            batch_attn_merge_kernel<<<(items + 7) / 8, 256, 0, s>>>(b->att_part, b->attn, B, c.num_kv_heads, GQ, b->S,
-                                                                   hd, oimg);
-            BT_CUDA_CHECK(cudaGetLastError());
+            BT_CUDA_CHECK(launch_pdl(batch_attn_merge_kernel, dim3((items + 7) / 8), dim3(256), 0, s, true,
+                                     (const float*)b->att_part, b->attn, B, c.num_kv_heads, GQ, b->S, hd, oimg));
             if (!oimg) BT_CUDA_CHECK(launch_token_image(b->attn, nullptr, nullptr, B, Q, b->img[1], nullptr, nullptr, s));
         }
         BT_CUDA_CHECK(launch_gemm_tokens(UnitW{Ld.o, D, unit_rows(D), Q}, gin(b->img[1], nullptr, 0.0f),
@@ -466,10 +468,9 @@ int enqueue_batch_step(bt_batch* b, cudaStream_t s) {
     const uint32_t nob = unit_rows(V) / 32;
     BT_CUDA_CHECK(launch_gemm_tokens(UnitW{e->head, V, unit_rows(V), D}, gin(b->img[0], b->ss, c.rms_norm_eps),
                                      GEpiLogits{b->logits, b->am_val, b->am_idx, V, nob}, err, nsm, s));
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-    batch_finish_kernel<<<(B + 7) / 8, 256, 0, s>>>(b->am_val, b->am_idx, nob, B, b->max_seq, b->pos, b->cur,
-                                                    b->n_fixed, b->last_am, b->tok_hist);
-    BT_CUDA_CHECK(cudaGetLastError());
+    BT_CUDA_CHECK(launch_pdl(batch_finish_kernel, dim3((B + 7) / 8), dim3(256), 0, s, true, (const float*)b->am_val,
+                             (const uint32_t*)b->am_idx, nob, B, b->max_seq, b->pos, b->cur,
+                             (const uint32_t*)b->n_fixed, b->last_am, b->tok_hist));
     return BT_OK;
 }
 

@@ -330,6 +330,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tokens_kernel(UnitW W, Gemm
     uint8_t* a16 = smem + (size_t)kGMaxStages * kGStageBytes;
     float* exch = reinterpret_cast<float*>(a16 + (size_t)kGA16Slots * kGA16);
 
+    // launched as a programmatic dependent of the previous kernel: the set-up and an L2
+    // prefetch of the first weight stages overlap that kernel's tail; nothing the previous
+    // kernels write is read (or written) before pdl_wait()
+    pdl_trigger();
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
@@ -353,6 +357,15 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tokens_kernel(UnitW W, Gemm
     __syncthreads();
     tcgen05_fence_after();
     const uint32_t tmem = s_tmem;
+    if (threadIdx.x == 0 && blockIdx.x < units) {
+        // the weight tiles of this CTA's first NS stages (weights are never written)
+        const uint32_t u = blockIdx.x, g = (u / KS) / NTG;
+        uint32_t bs, be;
+        split_blocks(NB, u % KS, KS, bs, be);
+        const uint32_t nb = min(be - bs, NS * kGStageBlocks);
+        if (nb) bulk_prefetch_l2(W.units + ((size_t)g * NB + bs) * kTileBytes, nb * kTileBytes);
+    }
+    pdl_wait();
 
     if (warp == 0) {
         // ---------------- producer
@@ -561,6 +574,8 @@ static __global__ void __launch_bounds__(256) token_image_kernel(const float* __
                                                           const uint32_t* __restrict__ tokens,
                                                           const float* __restrict__ w, uint32_t T, uint32_t K,
                                                           uint8_t* img, float* ss, float* x_out) {
+    pdl_trigger();
+    pdl_wait();
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t NB = K / 32;
     const uint64_t item = (uint64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -582,6 +597,8 @@ static __global__ void __launch_bounds__(256) token_image_kernel(const float* __
 // tile, token group, 16 tokens), warp q holding rows 32 q .. 32 q + 31.
 template <class Epi>
 __global__ void __launch_bounds__(128) gemm_reduce_kernel(UnitW W, GemmIn in, Epi epi) {
+    pdl_trigger();
+    pdl_wait();  // the splits' partial sums
     __shared__ float ex[16 * 64];
     const uint32_t q = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t NTG = token_groups(in.T), NB = W.K / kTileK;
@@ -617,12 +634,12 @@ __global__ void __launch_bounds__(128) gemm_reduce_kernel(UnitW W, GemmIn in, Ep
 
 inline uint32_t gemm_stages() { return (uint32_t)kGMaxStages; }
 
-// K-splits of a GEMM: enough units to give every SM one (at least 8 blocks per
-// split), within the workspace; 1 when there is no workspace.
+// K-splits of a GEMM: as many as keep every unit on an SM of its own (at least
+// 8 blocks per split), within the workspace; 1 when there is no workspace.
 inline uint32_t gemm_splits(uint32_t Mp, uint32_t K, uint32_t T, uint32_t nsm, size_t part_floats) {
     const uint32_t units = (Mp / kTileRows) * token_groups(T), NB = K / kTileK;
     if (units == 0 || units >= nsm || part_floats == 0) return 1;
-    uint32_t ks = (nsm + units - 1) / units;
+    uint32_t ks = nsm / units;  // KS * units <= nsm: no CTA takes two units
     ks = ks < NB / 8 ? ks : NB / 8;
     while (ks > 1 && (size_t)ks * T * Mp > part_floats) --ks;
     return ks < 1 ? 1 : ks;
@@ -652,11 +669,11 @@ cudaError_t launch_gemm_tokens(const UnitW& W, const GemmIn& in_, const Epi& epi
         attr_set[dev] = true;
     }
     const uint32_t grid = units < nsm ? units : nsm;
-    cudaError_t ce = launch_pdl(kern, dim3(grid), dim3(kGThreads), (size_t)kGSmem, s, false, W, in, epi,
+    cudaError_t ce = launch_pdl(kern, dim3(grid), dim3(kGThreads), (size_t)kGSmem, s, true, W, in, epi,
                                 gemm_stages(), err);
     if (ce != cudaSuccess || in.KS == 1) return ce;
     const uint32_t reduce_ctas = (W.Mp / kTileRows) * token_groups(in.T) * (kGTok / 16);
-    return launch_pdl(gemm_reduce_kernel<Epi>, dim3(reduce_ctas), dim3(128), 0, s, false, W, in, epi);
+    return launch_pdl(gemm_reduce_kernel<Epi>, dim3(reduce_ctas), dim3(128), 0, s, true, W, in, epi);
 }
 
 }  // namespace bt

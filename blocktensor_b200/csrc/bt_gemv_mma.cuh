@@ -504,7 +504,7 @@ constexpr uint32_t kAccBatch = 1;
 // Before a tile of a new row tile, flush() hands acc on (and must zero it and
 // advance cur_g).  s/ph: the ring position, carried by the caller.
 struct NoStageHook {
-    __device__ void operator()(uint32_t, uint32_t) const {}
+    __device__ void operator()(uint32_t, uint32_t, float = 0.0f) const {}
 };
 
 template <class Flush, class Hook = NoStageHook>
@@ -556,16 +556,31 @@ __device__ __forceinline__ void acc_stages(uint32_t u0, uint32_t u1, uint32_t NB
                 bs[t] = blk ? blk[bt] : 1.0f;
                 if (++bt == NB) bt = 0;
             }
+            hook(j + k, 7, [&] {
+                float z = 0.0f;  // every digit sum and factor (the timestamp waits for them)
 #pragma unroll
-            for (uint32_t t = 0; t < kStageTiles; ++t) {
-                if (t < nt[k]) {
-                    while (cur_g < g) flush();
-                    acc = fmaf(sc[k][t] * bs[t], y[t], acc);  // weight scale x the block's factor
+                for (uint32_t t = 0; t < kStageTiles; ++t) z += y[t] + bs[t];
+                return z;
+            }());
+            if (cur_g == g && b + nt[k] <= NB) {
+                // no row tile ends before the stage's last tile: one FMA chain, no flush
+#pragma unroll
+                for (uint32_t t = 0; t < kStageTiles; ++t)
+                    if (t < nt[k]) acc = fmaf(sc[k][t] * bs[t], y[t], acc);  // weight scale x the block's factor
+                b += kStageTiles;
+                while (b >= NB) { b -= NB; ++g; }
+            } else {
+#pragma unroll
+                for (uint32_t t = 0; t < kStageTiles; ++t) {
+                    if (t < nt[k]) {
+                        while (cur_g < g) flush();
+                        acc = fmaf(sc[k][t] * bs[t], y[t], acc);
+                    }
+                    if (++b == NB) { b = 0; ++g; }
                 }
-                if (++b == NB) { b = 0; ++g; }
             }
         }
-        hook(j, 6);
+        hook(j, 6, acc);
     }
 }
 

@@ -61,6 +61,14 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
+// The same clock, read only after `dep` is computed (a register input of the
+// read), so that a timestamp taken after some arithmetic is not moved before it.
+__device__ __forceinline__ uint64_t global_ns_after(float dep) {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer; // %1" : "=l"(t) : "f"(dep));
+    return t;
+}
+
 // Bounded wait for the phase with parity `parity`; false (and *err set) on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
     if (mbar_try_wait(bar, parity)) return true;

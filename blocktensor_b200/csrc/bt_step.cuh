@@ -100,15 +100,17 @@ enum : uint32_t {
 // the stage's copy, [1] issuer 1 sees it landed, [2] accumulator warp 5 sees
 // its MMAs complete, [3] that warp has read the results and releases the slot,
 // [4] issuer 1 has issued and committed its MMAs of the stage, [5] accumulator
-// warp 5 starts waiting for the stage's MMAs, [6] it has added the stage's sums.
+// warp 5 starts waiting for the stage's MMAs, [6] it has added the stage's sums,
+// [7] it has formed the stage's digit sums (before adding them).
 constexpr uint32_t kStageTraceMax = 2048;
 constexpr uint32_t kStageSlots = 8;
 
-__device__ __forceinline__ void stage_trace_at(const StepArgs& a, uint32_t P, uint32_t stage, uint32_t slot) {
+__device__ __forceinline__ void stage_trace_at(const StepArgs& a, uint32_t P, uint32_t stage, uint32_t slot,
+                                               float dep = 0.0f) {
 #ifdef BT_STAGE_TRACE
     if (a.trace && stage < kStageTraceMax)
         a.trace[(size_t)P * gridDim.x * kTraceSlots + ((size_t)blockIdx.x * kStageTraceMax + stage) * kStageSlots +
-                slot] = global_ns();
+                slot] = global_ns_after(dep);
 #endif
 }
 
@@ -1111,11 +1113,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
                 ++cur_g;
             };
 #ifdef BT_STAGE_TRACE
-            auto st_hook = [&](uint32_t j, uint32_t slot) {
-                if (warp == kAccWarp0 && lane == 0) stage_trace_at(a, P, rcount + j, slot);
+            auto st_hook = [&](uint32_t j, uint32_t slot, float dep = 0.0f) {
+                if (warp == kAccWarp0 && lane == 0) stage_trace_at(a, P, rcount + j, slot, dep);
             };
 #else
-            auto st_hook = [](uint32_t, uint32_t) {};
+            auto st_hook = [](uint32_t, uint32_t, float = 0.0f) {};
 #endif
             acc_stages(gm.u0, gm.u1, NB, gm.nstages, ring, NS, taddr, row, blk, mma_done, empty, rs, rph, ok, err, acc,
                        cur_g, flush, st_hook);
