@@ -25,8 +25,10 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 using namespace bt;
@@ -115,8 +117,6 @@ struct GEpiLogits {
 __global__ void batch_finish_kernel(const float* __restrict__ pv, const uint32_t* __restrict__ pi, uint32_t nob,
                                     uint32_t n_seq, uint32_t max_seq, uint32_t* pos, uint32_t* cur,
                                     const uint32_t* n_fixed, uint32_t* last_am, uint32_t* tok_hist) {
-    pdl_trigger();
-    pdl_wait();  // the head GEMM's argmax partials
     const uint32_t s = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (s >= n_seq) return;
     float bv = -INFINITY;
@@ -148,9 +148,10 @@ __global__ void batch_finish_kernel(const float* __restrict__ pv, const uint32_t
 // shared memory and the split's written to part (l = 0: no keys).
 // The CTA's partial of a split: its 8 warps' (m, l, o) [8][GQ][HD + 2] in shared
 // memory merged (empty warps, l = 0, skipped) into out[GQ][HD + 2].
-__device__ __forceinline__ void cta_merge_partials(const float* wm, float* out, uint32_t GQ, uint32_t HD) {
+__device__ __forceinline__ void cta_merge_partials(const float* wm, float* out, uint32_t GQ, uint32_t HD,
+                                                   uint32_t tid = threadIdx.x, uint32_t nthreads = blockDim.x) {
     const uint32_t pstride = HD + 2;
-    for (uint32_t e = threadIdx.x; e < GQ * HD; e += blockDim.x) {
+    for (uint32_t e = tid; e < GQ * HD; e += nthreads) {
         const uint32_t g = e / HD, d = e % HD;
         float M = -INFINITY;
         for (uint32_t ww = 0; ww < 8; ++ww) {
@@ -181,12 +182,11 @@ struct BatchAttnArgs {
     float* part;             // [B][KVH][S][GQ][hd + 2]
     uint32_t S, kps, KVH, GQ, hd, max_seq;
     float scale;
+    uint32_t* err;           // set when a bounded wait gives up
 };
 
 template <int NV, int GQM, typename KVT>
 __global__ void __launch_bounds__(256) batch_attn_kernel(BatchAttnArgs a) {
-    pdl_trigger();
-    pdl_wait();  // q and the appended K/V rows of the qkv GEMM
     extern __shared__ float wm[];  // [8 warps][GQ][hd + 2]
     constexpr int BW = 16 / RowWords<NV, KVT>::W / (GQM > 1 ? 2 : 1);
     constexpr int B = BW > 8 ? 8 : (BW < 2 ? 2 : BW);
@@ -283,8 +283,6 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(BatchAttnArgs a) {
 // warps take 16-key tiles of the split round robin.
 template <int HD, typename KVT>
 __global__ void __launch_bounds__(256, (HD == 64 && sizeof(KVT) == 2) ? 2 : 1) batch_attn_mma_kernel(BatchAttnArgs a) {
-    pdl_trigger();
-    pdl_wait();  // q and the appended K/V rows of the qkv GEMM
     extern __shared__ float wm[];  // [8 warps][GQ][HD + 2]
     const uint32_t lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const uint32_t sp = blockIdx.x, kvh = blockIdx.y, s = blockIdx.z;
@@ -325,6 +323,114 @@ __global__ void __launch_bounds__(256, (HD == 64 && sizeof(KVT) == 2) ? 2 : 1) b
     cta_merge_partials(wm, out, GQ, HD);
 }
 
+// fp16 caches: a producer warp (warp 8) streams the split's K and V rows into a
+// ring of shared-memory stages of 64 keys with bulk copies (one per contiguous
+// run of rows: the whole stage, or a page's piece of it), and the 8 consumer
+// warps take the 16-key tiles round robin (tile i: warp i mod 8; stage j's
+// four tiles go to four warps, which release it), the products on f16 MMAs
+// (GqaWarp16).  Copies run NS stages ahead of the slowest consumer, so the
+// split's rows stream at the copy engine's pace instead of one 4 KB tile per
+// warp and round trip.
+constexpr uint32_t kAttnStageKeys = 64;
+template <int HD>
+constexpr uint32_t attn_bulk_stages() { return HD == 64 ? 4 : 5; }
+template <int HD>
+constexpr size_t attn_bulk_smem(uint32_t GQ) {
+    // ring [NS][K | V][64 keys][HD] halves, the warps' partials [8][GQ][HD + 2], q's fragments, q's exponents
+    return (size_t)attn_bulk_stages<HD>() * 2 * kAttnStageKeys * HD * 2 + (size_t)8 * GQ * (HD + 2) * 4 +
+           (size_t)32 * (HD / 16) * 16 + 8 * 4;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(288, HD == 64 ? 2 : 1) batch_attn_bulk_kernel(BatchAttnArgs a) {
+    constexpr uint32_t NS = attn_bulk_stages<HD>();
+    constexpr uint32_t RB = HD * 2;                    // bytes per cache row
+    constexpr uint32_t SB = kAttnStageKeys * RB;       // K (or V) bytes of a stage
+    extern __shared__ __align__(128) uint8_t sm[];
+    __shared__ __align__(8) uint64_t full[NS], empty[NS];
+    const uint32_t lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const uint32_t sp = blockIdx.x, kvh = blockIdx.y, s = blockIdx.z;
+    const uint32_t GQ = a.GQ, pstride = HD + 2;
+    const uint32_t c = min(a.pos[s] + 1, a.max_seq);
+    const uint32_t t0 = sp * a.kps, t1 = min(c, t0 + a.kps);
+    float* out = a.part + ((((size_t)s * a.KVH + kvh) * a.S + sp) * GQ) * pstride;
+    if (t0 >= t1) {
+        for (uint32_t g = threadIdx.x; g < GQ; g += blockDim.x) {
+            out[(size_t)g * pstride] = -INFINITY;
+            out[(size_t)g * pstride + 1] = 0.0f;
+        }
+        return;
+    }
+    uint8_t* ring = sm;
+    float* wm = reinterpret_cast<float*>(sm + (size_t)NS * 2 * SB);
+    using GW = GqaWarp16<HD>;
+    uint4* qs = reinterpret_cast<uint4*>(wm + (size_t)8 * GQ * pstride);
+    int* qe = reinterpret_cast<int*>(qs + 32 * GW::KSTEPS);
+    const uint32_t nst = (t1 - t0 + kAttnStageKeys - 1) / kAttnStageKeys;
+    if (threadIdx.x == 0) {
+        for (uint32_t i = 0; i < NS; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 4);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const KVMap map = a.map;
+    if (w == 8) {
+        // ---------------- producer
+        if (lane == 0) {
+            const uint8_t* kc = static_cast<const uint8_t*>(a.kc);
+            const uint8_t* vc = static_cast<const uint8_t*>(a.vc);
+            const uint32_t run_max = map.paged() ? (1u << map.page_shift) : 0xFFFFFFFFu;
+            bool ok = true;
+            for (uint32_t j = 0; j < nst && ok; ++j) {
+                const uint32_t slot = j % NS;
+                if (j >= NS) ok = mbar_wait(&empty[slot], ((j / NS) - 1) & 1, a.err);
+                if (!ok) break;
+                const uint32_t k0 = t0 + j * kAttnStageKeys, k1 = min(t1, k0 + kAttnStageKeys);
+                mbar_expect_tx(&full[slot], 2 * (k1 - k0) * RB);
+                uint8_t* dk = ring + (size_t)slot * 2 * SB;
+                for (uint32_t t = k0; t < k1;) {
+                    // rows t .. t + n - 1 are contiguous (one sequence's head, or one page's piece)
+                    const uint32_t n = min(k1 - t, run_max - (t & (run_max - 1u)));
+                    const size_t off = map.row(s, kvh, t) * 2;
+                    bulk_g2s(dk + (size_t)(t - k0) * RB, kc + off, n * RB, &full[slot]);
+                    bulk_g2s(dk + SB + (size_t)(t - k0) * RB, vc + off, n * RB, &full[slot]);
+                    t += n;
+                }
+            }
+            // the ring's copies still in flight land before the CTA may end
+            const uint32_t first = nst > NS ? nst - NS : 0;
+            for (uint32_t j = first; j < nst && ok; ++j) ok = mbar_wait(&full[j % NS], (j / NS) & 1, a.err);
+        }
+        return;
+    }
+    // ---------------- consumers (warps 0-7)
+    auto csync = []() { asm volatile("bar.sync 1, 256;" ::: "memory"); };
+    const float* qh = a.q + (size_t)s * ((size_t)a.KVH * GQ * HD) + (size_t)kvh * GQ * HD;
+    GW::head_exponent(qe, qh, GQ, w, lane);
+    csync();
+    GW::stage_q(qs, qh, qe, GQ, threadIdx.x, 256);
+    csync();
+    GW st;
+    st.init(GQ, lane, qs, qe);
+    bool ok = true;
+    for (uint32_t i = w; i < 4 * nst; i += 8) {
+        const uint32_t j = i >> 2, slot = j % NS;
+        if (ok) ok = mbar_wait(&full[slot], (j / NS) & 1, a.err);
+        const uint32_t kb = t0 + j * kAttnStageKeys, k0 = t0 + 16 * i;
+        const __half* ks = reinterpret_cast<const __half*>(ring + (size_t)slot * 2 * SB);
+        typename GW::Tile f;
+        st.load_s(f, ks, ks + SB / 2, kb, k0, ok ? t1 : 0);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);  // the tile is in registers
+        st.compute(f, k0, ok ? t1 : 0, a.scale);
+    }
+    st.store(wm + (size_t)w * GQ * pstride, GQ);
+    csync();
+    cta_merge_partials(wm, out, GQ, HD, threadIdx.x, 256);
+}
+
 // attn[s][h hd + d] from the splits of (s, kv head, query head): the splits'
 // maxima and sums first (lane i holds split i, i + 32, ...), then o as the
 // weighted sum over the splits in split order.  One warp per (sequence, query
@@ -332,8 +438,6 @@ __global__ void __launch_bounds__(256, (HD == 64 && sizeof(KVT) == 2) ? 2 : 1) b
 // block of the o-proj input) it also writes the o-proj GEMM's token image.
 __global__ void batch_attn_merge_kernel(const float* __restrict__ part, float* __restrict__ attn, uint32_t B,
                                         uint32_t KVH, uint32_t GQ, uint32_t S, uint32_t hd, uint8_t* img) {
-    pdl_trigger();
-    pdl_wait();  // the splits' partials
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t item = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
     const uint32_t H = KVH * GQ;
@@ -392,7 +496,7 @@ cudaError_t launch_batch_attn_t(const BatchAttnArgs& a, uint32_t B, cudaStream_t
         const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    return launch_pdl(kern, dim3(a.S, a.KVH, B), dim3(256), smem, st, true, a);
+    return launch_pdl(kern, dim3(a.S, a.KVH, B), dim3(256), smem, st, false, a);
 }
 
 template <int HD, typename KVT>
@@ -404,14 +508,28 @@ cudaError_t launch_batch_attn_mma(const BatchAttnArgs& a, uint32_t B, cudaStream
         const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    return launch_pdl(kern, dim3(a.S, a.KVH, B), dim3(256), smem, st, true, a);
+    return launch_pdl(kern, dim3(a.S, a.KVH, B), dim3(256), smem, st, false, a);
+}
+
+template <int HD>
+cudaError_t launch_batch_attn_bulk(const BatchAttnArgs& a, uint32_t B, cudaStream_t st) {
+    const size_t smem = attn_bulk_smem<HD>(a.GQ);
+    auto kern = batch_attn_bulk_kernel<HD>;
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(kern, dim3(a.S, a.KVH, B), dim3(288), smem, st, false, a);
 }
 
 template <typename KVT>
 cudaError_t launch_batch_attn(const BatchAttnArgs& a, uint32_t B, cudaStream_t st) {
-    // the tensor-core kernel for head_dim 64 / 128 and up to 8 query heads per KV head
-    if (a.GQ <= 8 && a.hd == 64) return launch_batch_attn_mma<64, KVT>(a, B, st);
-    if (a.GQ <= 8 && a.hd == 128) return launch_batch_attn_mma<128, KVT>(a, B, st);
+    // the tensor-core kernels for head_dim 64 / 128 and up to 8 query heads per KV head
+    if constexpr (sizeof(KVT) == 2) {
+        if (a.GQ <= 8 && a.hd == 64) return launch_batch_attn_bulk<64>(a, B, st);
+        if (a.GQ <= 8 && a.hd == 128) return launch_batch_attn_bulk<128>(a, B, st);
+    } else {
+        if (a.GQ <= 8 && a.hd == 64) return launch_batch_attn_mma<64, KVT>(a, B, st);
+        if (a.GQ <= 8 && a.hd == 128) return launch_batch_attn_mma<128, KVT>(a, B, st);
+    }
     const bool mha = a.GQ == 1;
 #define BT_BATCH_ATTN(NV_)                                                                               \
     return mha ? launch_batch_attn_t<NV_, 1, KVT>(a, B, st) : launch_batch_attn_t<NV_, 16 / NV_, KVT>(a, B, st)
@@ -447,13 +565,13 @@ int enqueue_batch_step(bt_batch* b, cudaStream_t s) {
                                              epi, err, nsm, s));
         }
         BatchAttnArgs aa{b->q, kl, vl, b->map, b->pos, b->att_part, b->S, b->kps, c.num_kv_heads, GQ, hd,
-                         b->max_seq, 1.0f / std::sqrt((float)hd)};
+                         b->max_seq, 1.0f / std::sqrt((float)hd), err};
         BT_CUDA_CHECK(launch_batch_attn<KVT>(aa, B, s));
         {
             const uint32_t items = B * c.num_heads;
             // the merge writes the o-proj input's token image too when a head is whole 32-blocks
             uint8_t* oimg = hd % 32 == 0 ? b->img[1] : nullptr;
-            BT_CUDA_CHECK(launch_pdl(batch_attn_merge_kernel, dim3((items + 7) / 8), dim3(256), 0, s, true,
+            BT_CUDA_CHECK(launch_pdl(batch_attn_merge_kernel, dim3((items + 7) / 8), dim3(256), 0, s, false,
                                      (const float*)b->att_part, b->attn, B, c.num_kv_heads, GQ, b->S, hd, oimg));
             if (!oimg) BT_CUDA_CHECK(launch_token_image(b->attn, nullptr, nullptr, B, Q, b->img[1], nullptr, nullptr, s));
         }
@@ -468,7 +586,7 @@ int enqueue_batch_step(bt_batch* b, cudaStream_t s) {
     const uint32_t nob = unit_rows(V) / 32;
     BT_CUDA_CHECK(launch_gemm_tokens(UnitW{e->head, V, unit_rows(V), D}, gin(b->img[0], b->ss, c.rms_norm_eps),
                                      GEpiLogits{b->logits, b->am_val, b->am_idx, V, nob}, err, nsm, s));
-    BT_CUDA_CHECK(launch_pdl(batch_finish_kernel, dim3((B + 7) / 8), dim3(256), 0, s, true, (const float*)b->am_val,
+    BT_CUDA_CHECK(launch_pdl(batch_finish_kernel, dim3((B + 7) / 8), dim3(256), 0, s, false, (const float*)b->am_val,
                              (const uint32_t*)b->am_idx, nob, B, b->max_seq, b->pos, b->cur,
                              (const uint32_t*)b->n_fixed, b->last_am, b->tok_hist));
     return BT_OK;
@@ -617,9 +735,23 @@ int batch_create(bt_engine* e, uint32_t n_seq, uint32_t max_seq, int kv_dtype, u
     const uint32_t k0 = std::max(D, Q), k1 = std::max(F, Q);
     if ((rc = dev_alloc(b->allocs, &b->img[0], token_image_bytes(n_seq, k0), "token image"))) return cleanup(rc);
     if ((rc = dev_alloc(b->allocs, &b->img[1], token_image_bytes(n_seq, k1), "token image"))) return cleanup(rc);
-    // attention splits of at most 256 keys (per sequence, KV head)
-    b->kps = 256;
-    b->S = (max_seq + b->kps - 1) / b->kps;
+    // attention splits (per sequence and KV head) of kps keys, a multiple of 128 (the 8 warps'
+    // 16-key tiles): about 6 splits per SM over the batch's (sequence, KV head) pairs at
+    // max_seq (64 TinyLlama-shaped sequences of up to 4k keys: 1152; measured 256, 512, 1024,
+    // 1408, 2048: 14.2k, 15.0k, 15.1k, 14.6k, 14.6k tokens/s); BT_BATCH_KPS (a multiple of 16)
+    // overrides
+    {
+        const uint32_t pairs = n_seq * c.num_kv_heads, tiles = (max_seq + 127) / 128;
+        uint32_t S = (6 * e->num_sms + pairs - 1) / pairs;
+        S = std::max(1u, std::min(S, tiles));
+        b->kps = (max_seq + S - 1) / S;
+        b->kps = (b->kps + 127) / 128 * 128;
+        if (const char* v = std::getenv("BT_BATCH_KPS")) {
+            const long k = std::atol(v);
+            if (k >= 16 && k <= 65536 && k % 16 == 0) b->kps = (uint32_t)k;
+        }
+        b->S = (max_seq + b->kps - 1) / b->kps;
+    }
     if ((rc = dev_alloc(b->allocs, &b->att_part, (size_t)n_seq * c.num_kv_heads * b->S * GQ * (hd + 2), "splits")))
         return cleanup(rc);
     // split-K partials: a GEMM with fewer units than SMs is cut into up to about two units per SM

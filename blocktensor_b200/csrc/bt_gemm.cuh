@@ -307,6 +307,29 @@ struct GemmIn {
     uint32_t KS = 1;       // set by launch_gemm_tokens
 };
 
+// Sum of the KS splits' partials of rows r, tokens tok0 .. tok0 + nvalid - 1, in
+// split order: F splits at a time, the 16 tokens' loads of all F in flight together.
+template <int F = 4>
+__device__ __forceinline__ void sum_splits(float (&v)[16], const GemmIn& in, uint32_t Mp, uint32_t r, uint32_t tok0,
+                                           uint32_t nvalid) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+    for (uint32_t ks0 = 0; ks0 < in.KS; ks0 += F) {
+        float t[F][16];
+#pragma unroll
+        for (int k = 0; k < F; ++k) {
+            const float* pk = in.part + ((size_t)(ks0 + k) * in.T + tok0) * Mp + r;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                t[k][i] = (ks0 + k < in.KS && (uint32_t)i < nvalid) ? __ldcg(pk + (size_t)i * Mp) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < F; ++k)
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] += t[k][i];
+    }
+}
+
 // Blocks [b0, b1) of K-split ks of KS.
 __device__ __forceinline__ void split_blocks(uint32_t NB, uint32_t ks, uint32_t KS, uint32_t& b0, uint32_t& b1) {
     b0 = (uint32_t)(((uint64_t)NB * ks) / KS);
@@ -330,10 +353,6 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tokens_kernel(UnitW W, Gemm
     uint8_t* a16 = smem + (size_t)kGMaxStages * kGStageBytes;
     float* exch = reinterpret_cast<float*>(a16 + (size_t)kGA16Slots * kGA16);
 
-    // launched as a programmatic dependent of the previous kernel: the set-up and an L2
-    // prefetch of the first weight stages overlap that kernel's tail; nothing the previous
-    // kernels write is read (or written) before pdl_wait()
-    pdl_trigger();
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
@@ -357,15 +376,6 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tokens_kernel(UnitW W, Gemm
     __syncthreads();
     tcgen05_fence_after();
     const uint32_t tmem = s_tmem;
-    if (threadIdx.x == 0 && blockIdx.x < units) {
-        // the weight tiles of this CTA's first NS stages (weights are never written)
-        const uint32_t u = blockIdx.x, g = (u / KS) / NTG;
-        uint32_t bs, be;
-        split_blocks(NB, u % KS, KS, bs, be);
-        const uint32_t nb = min(be - bs, NS * kGStageBlocks);
-        if (nb) bulk_prefetch_l2(W.units + ((size_t)g * NB + bs) * kTileBytes, nb * kTileBytes);
-    }
-    pdl_wait();
 
     if (warp == 0) {
         // ---------------- producer
@@ -574,8 +584,6 @@ static __global__ void __launch_bounds__(256) token_image_kernel(const float* __
                                                           const uint32_t* __restrict__ tokens,
                                                           const float* __restrict__ w, uint32_t T, uint32_t K,
                                                           uint8_t* img, float* ss, float* x_out) {
-    pdl_trigger();
-    pdl_wait();
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t NB = K / 32;
     const uint64_t item = (uint64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -597,8 +605,6 @@ static __global__ void __launch_bounds__(256) token_image_kernel(const float* __
 // tile, token group, 16 tokens), warp q holding rows 32 q .. 32 q + 31.
 template <class Epi>
 __global__ void __launch_bounds__(128) gemm_reduce_kernel(UnitW W, GemmIn in, Epi epi) {
-    pdl_trigger();
-    pdl_wait();  // the splits' partial sums
     __shared__ float ex[16 * 64];
     const uint32_t q = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t NTG = token_groups(in.T), NB = W.K / kTileK;
@@ -608,23 +614,7 @@ __global__ void __launch_bounds__(128) gemm_reduce_kernel(UnitW W, GemmIn in, Ep
     const uint32_t tok0 = tg * kGTok + 16 * h;
     const uint32_t nvalid = tok0 < in.T ? min(16u, in.T - tok0) : 0u;
     float v[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = 0.0f;
-    // four splits at a time, the 16 tokens' loads of all four in flight together; added in split order
-    for (uint32_t ks0 = 0; ks0 < in.KS; ks0 += 4) {
-        float t[4][16];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float* pk = in.part + ((size_t)(ks0 + k) * in.T + tok0) * W.Mp + r;
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-                t[k][i] = (ks0 + k < in.KS && (uint32_t)i < nvalid) ? __ldcg(pk + (size_t)i * W.Mp) : 0.0f;
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] += t[k][i];
-    }
+    sum_splits<4>(v, in, W.Mp, r, tok0, nvalid);
     if (in.ss) scale_by_token_inv(v, in.ss, NB, W.K, in.eps, tok0, nvalid, lane);
     auto bar = []() { __syncthreads(); };
     epi.rows(r, r >> 5, tok0, nvalid, v, lane, q, ex, bar);
@@ -669,11 +659,11 @@ cudaError_t launch_gemm_tokens(const UnitW& W, const GemmIn& in_, const Epi& epi
         attr_set[dev] = true;
     }
     const uint32_t grid = units < nsm ? units : nsm;
-    cudaError_t ce = launch_pdl(kern, dim3(grid), dim3(kGThreads), (size_t)kGSmem, s, true, W, in, epi,
+    cudaError_t ce = launch_pdl(kern, dim3(grid), dim3(kGThreads), (size_t)kGSmem, s, false, W, in, epi,
                                 gemm_stages(), err);
     if (ce != cudaSuccess || in.KS == 1) return ce;
     const uint32_t reduce_ctas = (W.Mp / kTileRows) * token_groups(in.T) * (kGTok / 16);
-    return launch_pdl(gemm_reduce_kernel<Epi>, dim3(reduce_ctas), dim3(128), 0, s, true, W, in, epi);
+    return launch_pdl(gemm_reduce_kernel<Epi>, dim3(reduce_ctas), dim3(128), 0, s, false, W, in, epi);
 }
 
 }  // namespace bt

@@ -131,7 +131,7 @@ cudaError_t launch_token_image(const float* src, const uint32_t* tokens, const f
                                uint8_t* img, float* ss, float* x_out, cudaStream_t s) {
     const uint64_t items = (uint64_t)T * (K / 32);
     if (items == 0) return cudaSuccess;
-    return launch_pdl(token_image_kernel, dim3((unsigned)((items + 7) / 8)), dim3(256), 0, s, true, src, tokens, w, T,
+    return launch_pdl(token_image_kernel, dim3((unsigned)((items + 7) / 8)), dim3(256), 0, s, false, src, tokens, w, T,
                       K, img, ss, x_out);
 }
 

@@ -378,16 +378,31 @@ __device__ void attn_phase(const StepArgs& a, uint32_t l, uint8_t* scratch, uint
             if (GQ <= 8 && HD == 32 * NV) {  // NV = 2 also serves head_dim < 64: those stay on the CUDA cores
                 // grouped heads on the tensor cores: the warps take 16-key tiles round robin; q's
                 // fragments in shared memory after the warps' partials
-                using GW = GqaWarp<32 * NV, KVT, true>;
                 uint4* qs = reinterpret_cast<uint4*>(scratch + ((size_t)kDigitWarps * GQ * pstride * 4 + 15) / 16 * 16);
-                GW::stage_q(qs, a.q + (size_t)kvh * GQ * HD, GQ, tid, kDigitThreads);
-                digit_sync();
-                GW st;
-                st.init(nullptr, GQ, lane, qs);
+                const float* qh = a.q + (size_t)kvh * GQ * HD;
                 const size_t head_row0 = (size_t)kvh * a.max_seq;
                 auto row = [&](uint32_t t) { return (head_row0 + t) * (32 * NV); };
-                for (uint32_t k0 = t0 + 16 * w; k0 < t1; k0 += 16 * kDigitWarps) st.tile(kl, vl, k0, t1, a.scale, row);
-                st.store(wm + (size_t)w * GQ * pstride, GQ);
+                if constexpr (sizeof(KVT) == 2) {
+                    // fp16 cache: f16 MMAs, q in two fp16 terms scaled per head (exponents after the fragments)
+                    using GW = GqaWarp16<32 * NV>;
+                    int* qe = reinterpret_cast<int*>(qs + 32 * GW::KSTEPS);
+                    GW::head_exponent(qe, qh, GQ, w, lane);
+                    digit_sync();
+                    GW::stage_q(qs, qh, qe, GQ, tid, kDigitThreads);
+                    digit_sync();
+                    GW st;
+                    st.init(GQ, lane, qs, qe);
+                    for (uint32_t k0 = t0 + 16 * w; k0 < t1; k0 += 16 * kDigitWarps) st.tile(kl, vl, k0, t1, a.scale, row);
+                    st.store(wm + (size_t)w * GQ * pstride, GQ);
+                } else {
+                    using GW = GqaWarp<32 * NV, KVT, true>;
+                    GW::stage_q(qs, qh, GQ, tid, kDigitThreads);
+                    digit_sync();
+                    GW st;
+                    st.init(nullptr, GQ, lane, qs);
+                    for (uint32_t k0 = t0 + 16 * w; k0 < t1; k0 += 16 * kDigitWarps) st.tile(kl, vl, k0, t1, a.scale, row);
+                    st.store(wm + (size_t)w * GQ * pstride, GQ);
+                }
                 on_tensor_cores = true;
             }
         }

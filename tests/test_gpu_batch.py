@@ -118,6 +118,30 @@ def test_batch_tinyllama_width_two_layers(cuda, oracle):
     m.close()
 
 
+@pytest.mark.parametrize("kv_dtype", ["fp16", "fp32"])
+def test_batch_gqa_head_dim_128(cuda, oracle, kv_dtype):
+    """Eight query heads per KV head with head_dim 128 (the 70B shape's grouping): three
+    sequences with contexts up to ~270, so their keys span several attention splits, against
+    the oracle (fp16 caches on f16 tensor-core MMAs, fp32 caches on tf32)."""
+    d = dict(vocab=1000, dim=1024, hidden=2048, layers=2, heads=8, kv_heads=1, head_dim=128, max_seq=300)
+    cfg = cuda.model_config(*d.values())
+    ocfg = oracle.make_config(*d.values())
+    m = oracle.Model(ocfg, seed=17)
+    eng = cuda.TransformerEngine(cfg)
+    eng.load_pointers([(t.ptr, t.nbytes) for t in m.tensors()])
+    rng = np.random.default_rng(18)
+    prompts = [rng.integers(0, 1000, n).astype(np.uint32) for n in (3, 131, 240)]
+    n_gen = 32
+    fp16 = kv_dtype == "fp16"
+    toks, logits = run_batch(cuda, eng, prompts, n_gen, 300, cuda.BT_KV_FP16 if fp16 else cuda.BT_KV_FP32)
+    for s, p in enumerate(prompts):
+        want, lo = oracle_run(oracle, m, ocfg, p, n_gen, 300, fp16)
+        assert np.array_equal(toks[s], want[: len(toks[s])]), f"sequence {s}"
+        assert rel_l2(logits[s], lo) <= TOL, f"sequence {s}: logits relative error {rel_l2(logits[s], lo)}"
+    eng.close()
+    m.close()
+
+
 def test_batch_errors(cuda):
     d = dict(vocab=64, dim=64, hidden=128, layers=1, heads=2, kv_heads=2, head_dim=32, max_seq=16)
     eng = cuda.TransformerEngine(cuda.model_config(*d.values()))
