@@ -64,17 +64,25 @@ class ClockSampler:
         self.out = os.path.join("/tmp", f"bt_clocks_{os.getpid()}.csv")
 
     def start(self):
+        """Starts sampling every 50 ms and returns once the first sample is written (nvidia-smi
+        takes a while to come up), so samples cover the whole timed region that follows."""
         try:
             self.f = open(self.out, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
+            t0 = time.time()
+            while time.time() - t0 < 5.0 and self.proc.poll() is None:
+                if os.path.getsize(self.out) > 0:
+                    break
+                time.sleep(0.02)
         except Exception:
             self.proc = None
 
     def stop(self):
         if self.proc is None:
             return None
+        time.sleep(0.06)  # one more sample at the end of the region
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
