@@ -130,6 +130,10 @@ int plan_step(bt_engine* e) {
         const long n = std::atol(v);
         if (n >= 0 && n <= 64) e->step_pf = (uint32_t)n;
     }
+    if (const char* v = std::getenv("BT_STEP_MIN_TILES")) {
+        const long n = std::atol(v);
+        if (n >= 0 && n <= 4096) e->step_min_tiles = (uint32_t)n;
+    }
     if (const char* v = std::getenv("BT_STEP_EVICT_FIRST")) {
         if (v[0] != '0') e->step_flags |= kStepFlagEvictFirst;
         else e->step_flags &= ~kStepFlagEvictFirst;
@@ -240,6 +244,7 @@ int launch_step(bt_engine* e, bt_kv* kv, cudaStream_t s) {
     a.tmem_cols = e->step_tmem;
     a.scratch_off = e->step_scratch_off;
     a.pf_stages = e->step_pf;
+    a.min_tiles = e->step_min_tiles;
     a.flags = e->step_flags;
     a.trace = e->trace;
     const uint32_t grid = e->num_sms;

@@ -51,6 +51,11 @@ struct bt_engine {
     // stages of L2 prefetch ahead of the ring while the consumers are held up (BT_STEP_PF; off by
     // default: measured slower on the 7B step, the prefetched weights evict the K/V rows attention reads)
     uint32_t step_pf = 0;
+    // StepArgs::min_tiles: 32 tiles (4 stages) per CTA at least; the 7B-shaped o-proj at 1 GPU
+    // (4096 tiles) then runs on 128 CTAs, each row tile in 4 aligned pieces (481 -> 486 tokens/s),
+    // and under tensor parallelism the small per-rank matrices are cut into fewer pieces (4 GPUs:
+    // 510 -> 671 tokens/s); BT_STEP_MIN_TILES overrides (0: every SM)
+    uint32_t step_min_tiles = 32;
     uint32_t step_flags = 0;   // kStepFlag* options of the step kernel
     uint64_t* trace = nullptr; // per-phase timestamps of the last step ([5 L + 1][num_sms][kTraceSlots])
     bool taps_on = false;

@@ -77,6 +77,9 @@ struct StepArgs {
     // L2 prefetch of upcoming weight stages while the consumers are held up (0: off), and
     // kStepFlag* options
     uint32_t pf_stages, flags;
+    // fewest weight tiles a CTA takes in a GEMV phase (0: no floor): a small matrix then runs
+    // on U / min_tiles CTAs, its row tiles cut into fewer pieces
+    uint32_t min_tiles;
     // per-phase device timestamps (null: off): [P][G][kTraceSlots] of %globaltimer
     uint64_t* trace;
 };
@@ -127,17 +130,19 @@ __device__ __forceinline__ StepMat phase_mat(const StepArgs& a, uint32_t p) {
     return k == kPhQKV ? l.qkv : k == kPhO ? l.o : k == kPhGU ? l.gu : l.d;
 }
 
-// Tile range of CTA c in the stream-K split of matrix m over Gm = min(G, U)
-// CTAs (every CTA of the split owns at least one tile; CTAs c >= Gm own none).
+// Tile range of CTA c in the stream-K split of matrix m over Gm = min(G, U,
+// U / min_tiles) CTAs (every CTA of the split owns at least one tile; CTAs
+// c >= Gm own none).
 struct Geo {
     uint32_t NB, U, Gm, u0, u1, g_first, g_last, nstages;
 };
 
-__device__ __forceinline__ Geo phase_geo(const StepMat& m, uint32_t c, uint32_t G) {
+__device__ __forceinline__ Geo phase_geo(const StepMat& m, uint32_t c, uint32_t G, uint32_t min_tiles) {
     Geo r;
     r.NB = m.K / kTileK;
     r.U = (m.Mp / kTileRows) * r.NB;
-    r.Gm = r.U < G ? r.U : G;
+    const uint32_t gmax = min_tiles ? max(1u, r.U / min_tiles) : r.U;
+    r.Gm = gmax < G ? gmax : G;
     if (c >= r.Gm) {
         r.u0 = r.u1 = 0;
         r.g_first = 1;
@@ -166,7 +171,7 @@ __device__ __forceinline__ void cursor_settle(StageCursor& k, const StepArgs& a,
     for (; k.p < P; ++k.p) {
         if (phase_kind(k.p, a.L) == kPhAttn) continue;
         const StepMat mt = phase_mat(a, k.p);
-        const Geo gm = phase_geo(mt, c, G);
+        const Geo gm = phase_geo(mt, c, G, a.min_tiles);
         if (gm.nstages) {
             k.j = 0;
             k.nst = gm.nstages;
@@ -825,7 +830,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) decode_step_kernel(StepArgs a)
             }
             continue;
         }
-        const Geo gm = phase_geo(mt, c, G);
+        const Geo gm = phase_geo(mt, c, G, a.min_tiles);
         const uint32_t NB = mt.K / kTileK;
         const bool norm = kind == kPhQKV || kind == kPhGU || kind == kPhHead;
         // the input's digits: a bulk copy of the image the previous phase wrote, or built here
