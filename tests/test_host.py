@@ -46,3 +46,29 @@ def test_btmodel_truncated(tmp_path, oracle):
     p.write_bytes(data[:-10])
     with pytest.raises(RuntimeError):
         btmodel.read_btmodel(str(p))
+
+
+def test_stage_trace_summary():
+    """The stage-timeline summary picks the stages whose MMAs the accumulator saw inside the
+    phase and reports the intervals between the stamps (synthetic stamps, no GPU)."""
+    import numpy as np
+
+    from blocktensor_b200 import stage_trace as st
+
+    L, G = 12, 2
+    phase = np.zeros((5 * L + 1, G, 8), np.uint64)
+    stage = np.zeros((G, st.STAGE_TRACE_MAX, st.STAGE_SLOTS), np.uint64)
+    p = 5 * 10 + st.PHASES.index("gateup")
+    t0 = 1_000_000
+    phase[p, 0, 0], phase[p, 0, 3] = t0, t0 + 10_000
+    for i in range(4):  # stages 100..103, one every 700 ns
+        b = t0 + 1_000 + 700 * i
+        # copy, landed, seen, released, issued, wait start, added, sums
+        stage[0, 100 + i] = [b - 2_000, b - 500, b + 130, b + 290, b - 240, b, b + 580, b + 450]
+    stage[0, 99, 2] = t0 - 5  # seen before the phase: not one of its stages
+    out = st.summarize(phase, stage, 10, "gateup", 0)
+    lines = out.splitlines()
+    assert lines[0].startswith("CTA 0, layer 10 gateup: 4 stages, phase 10.00 us")
+    assert len(lines) == 2 + 4 + 1
+    assert "release to release 0.70" in lines[-1]
+    assert "wait 0.13" in lines[-1] and "adds 0.13" in lines[-1]
