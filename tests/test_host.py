@@ -72,3 +72,33 @@ def test_stage_trace_summary():
     assert len(lines) == 2 + 4 + 1
     assert "release to release 0.70" in lines[-1]
     assert "wait 0.13" in lines[-1] and "adds 0.13" in lines[-1]
+
+
+def test_phase_trace_summary():
+    """bench.py's per-phase summary of a step trace: durations, counter waits and tails from
+    synthetic stamps (every phase 10 us, CTAs passing their wait 1 us after the previous end,
+    the last CTA ending 2 us after the median one)."""
+    import importlib.util
+    import os
+
+    import numpy as np
+
+    spec = importlib.util.spec_from_file_location("bench", os.path.join(os.path.dirname(__file__), "..", "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    L, G = 4, 3
+    P = 5 * L + 1
+    tr = np.zeros((P, G, 8), np.uint64)
+    for p in range(P):
+        base = 1_000_000 + 10_000 * p
+        for c in range(G):
+            tr[p, c, 0] = base + 1_000                # passed the counter wait
+            tr[p, c, 1] = base + 2_000                # digits in shared memory
+            tr[p, c, 2] = base + 3_000                # first row tile's sums
+            tr[p, c, 3] = base + 8_000 + (2_000 if c == G - 1 else 0)  # end: the last CTA 2 us later
+            tr[p, c, 4] = base - 20_000               # first copy of the phase
+    res = bench.trace_summary(tr, L)
+    for k in ("qkv", "oproj", "gateup", "down"):
+        assert res[k]["dur"] == 10.0 and res[k]["wait"] == 1.0
+        assert res[k]["digits"] == 1.0 and res[k]["first"] == 1.0 and res[k]["tail"] == 2.0
+    assert res["step_us"] == round((float(tr[:, :, 3].max()) - float(tr[:, :, 0].min())) / 1000.0, 1)
